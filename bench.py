@@ -1,0 +1,406 @@
+"""Benchmark: ResNet-50 FP32 inference img/s (+ FFN FP16 tokens/s) on B200.
+
+One process per GPU (torchrun for N > 1), one Engine + ExecutionContext per
+GPU with replicated constants and a batch shard of 256 images per GPU (weak
+scaling, no collective on the data path). Each step is one pass of the
+compiled ResNet-50 (batch 256, 224x224, FP32) through
+ExecutionContext::RunAsync; the timed region is K steps bracketed by a
+barrier + device synchronize, timed with CUDA events on the launching
+stream, max over ranks. Inputs (154 MB per step) are larger than L2.
+
+The line also reports: the end-to-end rate through the C ABI with host
+buffers (pinned H2D of the step's images + D2H of the logits inside the
+timed region), the roofline of the dominant kernel family (the FP32
+convolutions), the FFN FP16 block (config 1: M=4096, H=768, I=3072), the
+PyTorch-eager CPU baseline on a bounded sample, and SM clocks sampled during
+the timed region.
+
+``--impl reference`` times the reference's CPU comparison path (the PyTorch
+eager ResNet-50 of the reference's benchmarks/resnet50_compare.py, restated
+in oracle/torch_ref.py) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+RN_BATCH_PER_GPU = 256
+FFN = dict(tokens=4096, hidden=768, inner=3072)
+
+
+def parse_args() -> argparse.Namespace:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--batch", type=int, default=RN_BATCH_PER_GPU, help="images per GPU")
+    p.add_argument("--no-ffn", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks() -> tuple[dict, str]:
+    if PEAKS_FILE.exists():
+        return json.loads(PEAKS_FILE.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the
+    timed region (200 ms period)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"ctb_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.device_index), "-lms", "200"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.out.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.strip()]
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        sm_max = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for name, value in zip(names, r[5:9]):
+                if value.strip().lower() == "active":
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(sm_max) if sm_max else None,
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+def dist_setup(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def kernel_launches_per_run(engine, ctx) -> int:
+    total = 0
+    for i, op in enumerate(engine.ops()):
+        cand = op["candidates"][ctx.selected_candidate(i)]
+        if cand == "view:flatten":
+            continue
+        total += 3 if cand == "unfused:conv_bn_relu" else (2 if cand.startswith("unfused:") else 1)
+    return total
+
+
+def resnet_work(batch: int) -> dict:
+    """Per-step algorithmic work of ResNet-50 at `batch` (FLOPs per conv
+    family and minimal bytes), from the layer table."""
+    from cutriton_b200.workloads import resnet50_layers
+
+    conv_flops = 0.0
+    conv_bytes = 0.0
+    h = 224
+    block_h = h
+    for kind, item in resnet50_layers():
+        if kind == "maxpool":
+            h = (h + 2 - 3) // 2 + 1
+            block_h = h
+            continue
+        if kind == "block_add":
+            block_h = h
+            continue
+        layer = item
+        in_h = block_h if layer.prefix.endswith(("_conv1", "_downsample")) else h
+        out_h = (in_h + 2 * layer.pad - layer.kernel) // layer.stride + 1
+        conv_flops += 2.0 * batch * out_h * out_h * layer.cout * layer.cin * layer.kernel ** 2
+        conv_bytes += 4.0 * (batch * layer.cin * in_h * in_h + layer.cout * layer.cin * layer.kernel ** 2
+                             + batch * layer.cout * out_h * out_h)
+        if not layer.prefix.endswith("_downsample"):
+            h = out_h
+    return {"conv_flops": conv_flops, "conv_bytes": conv_bytes,
+            "total_flops": conv_flops + 2.0 * batch * 2048 * 1000}
+
+
+def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
+    import torch
+
+    import cutriton_b200 as ct
+    from cutriton_b200 import workloads
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    batch = args.batch
+    weights = workloads.resnet50_weights("baseline", seed=0)
+    model = workloads.build_resnet50(weights, batch=batch)
+    engine = ct.build_engine(model, device_id=local, enable_cuda_graph=True, enable_profiling=True,
+                             enable_residual_fusion=True, tuning_mode=ct.TUNING_DISABLED)
+    ctx = engine.create_context()
+    x_host = workloads.resnet50_input(batch, seed=rank)
+    x = torch.from_numpy(x_host).to(device)
+    y = torch.empty(batch, 1000, device=device)
+    ctx.bind_tensor("input", x)
+    ctx.bind_tensor("output", y, output=True)
+    stream = torch.cuda.Stream(device)
+    for _ in range(max(3, args.warmup)):
+        ctx.run_async(stream.cuda_stream)
+        ctx.synchronize()
+
+    launches = kernel_launches_per_run(engine, ctx)
+    op_types = [o["op_type"] for o in engine.ops()]
+    conv_ops = [i for i, t in enumerate(op_types) if "Conv" in t]
+    conv_ms = []
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            ctx.run_async(stream.cuda_stream)
+            ctx.synchronize()  # the reference harness synchronizes every run
+            events = ctx.profile_events()
+            conv_ms.append(sum(events[i][1] for i in conv_ops))
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
+    clock_summary = clocks.summary()
+    ms_per_step = elapsed_ms / args.steps
+    value = world * batch * args.steps / (elapsed_ms / 1e3)
+
+    work = resnet_work(batch)
+    conv_ms_avg = float(np.mean(conv_ms))
+    achieved_tflops = work["conv_flops"] / (conv_ms_avg / 1e3) / 1e12
+    # FP32 convolutions run as 3xTF32 on the tensor cores: 3 TF32 MMAs (TF32
+    # = half the BF16 rate) per FP32 multiply-add, so the FP32-equivalent
+    # ceiling is bf16_tflops / 6 of the measured BF16 peak.
+    peak_tflops = peaks["bf16_tflops_sustained"] / 6.0
+    result = {
+        "value": value, "ms_per_step": ms_per_step, "launches_per_step": launches, "clocks": clock_summary,
+        "roofline": {
+            "bound": "tensor", "kernel": "FP32 convolution family (all conv ops of one step)",
+            "achieved": achieved_tflops, "peak": peak_tflops, "unit": "TFLOP/s",
+            "frac": achieved_tflops / peak_tflops,
+            "peak_basis": f"{peak_kind} bf16_tflops_sustained {peaks['bf16_tflops_sustained']} / 6 (3xTF32 FP32-equivalent)",
+            "conv_ms_per_step": conv_ms_avg, "algorithmic_gflop_per_step": work["conv_flops"] / 1e9,
+            "hbm_frac_at_min_bytes": (work["conv_bytes"] / (conv_ms_avg / 1e3) / 1e9) / peaks["hbm_gbs"],
+            "traffic": None,
+        },
+        "whole_net_tflops": work["total_flops"] / (ms_per_step / 1e3) / 1e12,
+    }
+
+    if not args.no_e2e:
+        pinned = torch.from_numpy(x_host).pin_memory()
+        host_out = np.empty((batch, 1000), np.float32)
+        host_in = pinned.numpy()
+        ctx.run_host({"input": host_in}, {"output": host_out}, stream=stream.cuda_stream)
+        barrier(world)
+        torch.cuda.synchronize()
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        steps = max(3, args.steps // 2)
+        for _ in range(steps):
+            ctx.run_host({"input": host_in}, {"output": host_out}, stream=stream.cuda_stream)
+        e_end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+        result["e2e"] = {"value": world * batch * steps / (e_ms / 1e3), "unit": "img/s",
+                         "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(host_out.nbytes),
+                         "path": "ctb_context_run_host (C ABI), pinned host buffers"}
+    return result
+
+
+def run_ffn(args, world, rank, local) -> dict:
+    import torch
+
+    import cutriton_b200 as ct
+    from cutriton_b200 import workloads
+
+    device = torch.device("cuda", local)
+    t, h, i = FFN["tokens"], FFN["hidden"], FFN["inner"]
+    w = workloads.ffn_weights(h, i, seed=0)
+    engine = ct.build_engine(workloads.build_ffn(w, t, h, i), device_id=local, enable_cuda_graph=True,
+                             enable_profiling=False, tuning_mode=ct.TUNING_DISABLED)
+    ctx = engine.create_context()
+    x = torch.from_numpy(workloads.ffn_input(t, h, seed=rank)).to(device)
+    y = torch.empty(t, h, dtype=torch.float16, device=device)
+    ctx.bind_tensor("x", x)
+    ctx.bind_tensor("output", y, output=True)
+    # L2 flush buffer (inputs of this config fit in L2).
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    stream = torch.cuda.Stream(device)
+    for _ in range(max(3, args.warmup)):
+        ctx.run_async(stream.cuda_stream)
+        ctx.synchronize()
+    steps = max(20, args.steps * 5)
+    times = []
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            flush.fill_(1.0)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            ctx.run_async(stream.cuda_stream)
+            e.record(stream)
+            ctx.synchronize()
+            times.append(s.elapsed_time(e))
+    med = max_over_ranks(float(np.median(times)), world)
+    flops = 4.0 * t * h * i
+    return {"metric": "FFN FP16 tokens/s (M=4096, H=768, I=3072)", "value": world * t / (med / 1e3),
+            "unit": "tokens/s", "ms_per_step": med, "tflops": flops / (med / 1e3) / 1e12,
+            "l2": "flushed (256 MB write) before every timed step"}
+
+
+def cpu_baseline(threads: int | None = None, batch: int = 8, steps: int = 2) -> dict:
+    import torch
+
+    from cutriton_b200 import workloads
+    from oracle import torch_ref
+
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    weights = workloads.resnet50_weights("baseline", seed=0)
+    x = workloads.resnet50_input(batch, seed=0)
+    torch_ref.resnet50_logits(x[:1], weights)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        torch_ref.resnet50_logits(x, weights)
+    dt = time.perf_counter() - t0
+    return {"value": batch * steps / dt, "unit": "img/s", "cores": threads, "kind": "port",
+            "sample": f"PyTorch eager FP32 ResNet-50 on CPU, {steps} x batch {batch} (bounded sample of the bs256 step)"}
+
+
+def base_line(args, world) -> dict:
+    return {
+        "metric": "ResNet-50 FP32 inference img/s (bs256 per GPU, 224x224)",
+        "unit": "img/s", "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) images, seeded Kaiming/BN/FC weights)",
+        "config": {"workload": "resnet50_fp32_inference", "model": "ResNet-50 v1.5", "global_batch": args.batch * world,
+                   "batch_per_gpu": args.batch, "image": "3x224x224 NCHW", "parallelism": f"dp{world} (batch shards)",
+                   "l2": "inputs larger than L2 (154 MB/step)", "cuda_graph": True, "residual_fusion": True},
+    }
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if rank != 0:
+            return
+        line = base_line(args, world)
+        line["impl"] = "reference"
+        import torch
+
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        from cutriton_b200 import workloads
+        from oracle import torch_ref
+
+        weights = workloads.resnet50_weights("baseline", seed=0)
+        batch = 8
+        x = workloads.resnet50_input(batch, seed=0)
+        for _ in range(max(1, min(args.warmup, 2))):
+            torch_ref.resnet50_logits(x[:2], weights)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            torch_ref.resnet50_logits(x, weights)
+        dt = time.perf_counter() - t0
+        value = batch * args.steps / dt
+        sample = f"PyTorch eager FP32 ResNet-50 on {threads} host threads, batch {batch} per step"
+        line.update({"value": value, "ms_per_step": dt / args.steps * 1e3, "n_gpus": 0,
+                     "config": {**line["config"], "batch_per_step": batch},
+                     "cpu_baseline": {"value": value, "unit": "img/s", "cores": threads, "kind": "port",
+                                      "sample": sample},
+                     "e2e": {"value": value, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+        print(json.dumps(line), flush=True)
+        return
+
+    world, rank, local = dist_setup(args)
+    peaks, peak_kind = load_peaks()
+    rn = run_resnet(args, world, rank, local, peaks, peak_kind)
+    ffn = None if args.no_ffn else run_ffn(args, world, rank, local)
+    if rank == 0:
+        line = base_line(args, world)
+        line.update({"value": rn["value"], "ms_per_step": rn["ms_per_step"], "roofline": rn["roofline"],
+                     "clocks": rn["clocks"], "gpu_launches": rn["launches_per_step"] * args.steps,
+                     "whole_net_tflops": rn["whole_net_tflops"]})
+        if "e2e" in rn:
+            line["e2e"] = rn["e2e"]
+        if ffn is not None:
+            line["ffn"] = ffn
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        line["peaks"] = peak_kind
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

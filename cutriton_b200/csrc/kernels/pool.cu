@@ -1,0 +1,59 @@
+// Pooling kernels over NCHW FP32.
+//
+// MaxPool follows python/cutriton/triton_kernels/resnet.py:159-182: window
+// maximum with out-of-range taps contributing -inf, padding taken from
+// pads[0] (top) and pads[1] (left). Comparisons are exact, so results are
+// bit-identical to any correct implementation. One thread per output; the
+// 3x3/2 windows of neighbouring threads overlap, so input rows are served
+// from L1 and HBM traffic stays near input + output bytes.
+//
+// GlobalAveragePool (resnet.py:185-198): one warp per (n, c) plane, lanes
+// stride the plane, warp-shuffle sum, then divide by H*W.
+
+#include <math_constants.h>
+
+#include "common.cuh"
+
+extern "C" __global__ void __launch_bounds__(256)
+ctb_max_pool_f32(const float* __restrict__ x, float* __restrict__ out, int n, int c, int h, int w,
+                 int out_h, int out_w, int kernel_h, int kernel_w, int stride_h, int stride_w,
+                 int pad_h, int pad_w, int dilation_h, int dilation_w, CTB_RESERVED_PARAMS) {
+  CTB_UNUSED_RESERVED();
+  const long long total = static_cast<long long>(n) * c * out_h * out_w;
+  const long long index = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= total) return;
+  const int ow = static_cast<int>(index % out_w);
+  long long rest = index / out_w;
+  const int oh = static_cast<int>(rest % out_h);
+  const long long plane = rest / out_h;  // n * c + channel
+  const float* src = x + plane * h * w;
+  float best = -CUDART_INF_F;
+  const int h0 = oh * stride_h - pad_h;
+  const int w0 = ow * stride_w - pad_w;
+  for (int kh = 0; kh < kernel_h; ++kh) {
+    const int ih = h0 + kh * dilation_h;
+    if (ih < 0 || ih >= h) continue;
+    for (int kw = 0; kw < kernel_w; ++kw) {
+      const int iw = w0 + kw * dilation_w;
+      if (iw < 0 || iw >= w) continue;
+      best = fmaxf(best, __ldg(src + static_cast<long long>(ih) * w + iw));
+    }
+  }
+  out[index] = best;
+}
+
+extern "C" __global__ void __launch_bounds__(256)
+ctb_global_average_pool_f32(const float* __restrict__ x, float* __restrict__ out, int n, int c, int h,
+                            int w, CTB_RESERVED_PARAMS) {
+  CTB_UNUSED_RESERVED();
+  const int warps_per_block = blockDim.x / 32;
+  const long long plane = static_cast<long long>(blockIdx.x) * warps_per_block + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (plane >= static_cast<long long>(n) * c) return;
+  const int spatial = h * w;
+  const float* src = x + plane * spatial;
+  float sum = 0.0f;
+  for (int i = lane; i < spatial; i += 32) sum += __ldg(src + i);
+  sum = ctb::warp_sum(sum);
+  if (lane == 0) out[plane] = sum / static_cast<float>(spatial);
+}

@@ -1,0 +1,261 @@
+"""nvcc-based Kernel SDK: kernel descriptors -> sm_100a cubins + pack.json v2.
+
+Replaces the reference's Triton AOT builder (python/cutriton/kernel_sdk/
+spec.py:7-187, builder.py:49-119). A :class:`KernelSpec` names a CUDA source,
+the ``extern "C"`` symbol, the ordered parameter list with the safe binding
+source of each parameter, the launch grid expression and the variants (each
+variant may set compile-time defines, warps and shared memory). Validation
+rejects the same unsafe inputs as the reference SDK: unknown argument
+sources or source fields, missing/misplaced ``runtime_reserved`` tail,
+anything but exactly one default variant, unknown grid or constraint kinds.
+
+Build time only: the runtime never imports Python.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import shutil
+from concurrent.futures import ThreadPoolExecutor
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Callable
+
+PACK_SCHEMA_VERSION = 2
+ABI_SCHEMA_VERSION = 2
+GENERATOR_VERSION = "b200-nvcc-1.0"
+PACK_NAME = "cutriton_sm100"
+PACK_VERSION = 1
+KERNEL_DIR = Path(__file__).resolve().parent / "csrc" / "kernels"
+
+_SOURCE_FIELDS = {
+    "input": {"kind", "index", "prepack"},
+    "output": {"kind", "index"},
+    "input_dim": {"kind", "index", "axis"},
+    "input_dim_product": {"kind", "index", "begin_axis"},
+    "output_dim": {"kind", "index", "axis"},
+    "output_numel": {"kind", "index"},
+    "input_numel": {"kind", "index"},
+    "attribute_i64": {"kind", "name", "alternate_name", "index", "default"},
+    "attribute_f64": {"kind", "name", "alternate_name", "index", "default"},
+    "literal_i32": {"kind", "default"},
+    "runtime_reserved": {"kind"},
+    "tensor_map": {"kind", "tensor", "index", "box", "swizzle", "prepack"},
+}
+_CONSTRAINT_FIELDS = {
+    "attribute_i64_eq": {"kind", "name", "value", "default"},
+    "input_count_eq": {"kind", "value"},
+    "tensor_rank_eq": {"kind", "source", "index", "value"},
+    "attribute_list_eq": {"kind", "name", "value", "default"},
+    "dim_multiple_of": {"kind", "source", "index", "axis", "value"},
+    "dim_le": {"kind", "source", "index", "axis", "value"},
+    "input_is_constant": {"kind", "index"},
+}
+_GRID_FIELDS = {
+    "literal": {"kind", "value"},
+    "input_dim": {"kind", "index", "axis"},
+    "output_dim": {"kind", "index", "axis"},
+    "input_numel": {"kind", "index"},
+    "output_numel": {"kind", "index"},
+    "meta": {"kind", "name"},
+    "ceil_div": {"kind", "args"},
+    "mul": {"kind", "args"},
+}
+_PREPACKS = {"transpose_2d", "conv_w_tf32x2_orsi", "gemm_w_tf32x2_nk"}
+
+
+@dataclass(frozen=True)
+class Arg:
+    name: str
+    type: str
+    source: dict[str, Any]
+
+
+@dataclass(frozen=True)
+class Variant:
+    variant_id: str
+    num_warps: int = 8
+    shared_memory_bytes: int = 0
+    meta: dict[str, int] = field(default_factory=dict)
+    defines: dict[str, str] = field(default_factory=dict)
+    default: bool = False
+    # Per-variant argument overrides (e.g. tensor-map boxes), by arg name.
+    arg_overrides: dict[str, dict[str, Any]] = field(default_factory=dict)
+    constraints: tuple[dict[str, Any], ...] = ()
+
+
+@dataclass(frozen=True)
+class KernelSpec:
+    kernel_id: str
+    op_type: str
+    version: int
+    source: str
+    symbol: str
+    arguments: tuple[Arg, ...]
+    grid: tuple[dict[str, Any], ...]
+    variants: tuple[Variant, ...]
+    dtype: str = "float32"
+    layout: str = ""
+    min_compute_capability: int = 100
+    constraints: tuple[dict[str, Any], ...] = ()
+
+    def validate(self) -> None:
+        if not self.kernel_id or not self.op_type or self.version <= 0 or not self.symbol:
+            raise ValueError("KernelSpec identity is incomplete")
+        if not self.variants or sum(v.default for v in self.variants) != 1:
+            raise ValueError(f"{self.kernel_id}: exactly one default variant is required")
+        if len({v.variant_id for v in self.variants}) != len(self.variants):
+            raise ValueError(f"{self.kernel_id}: duplicate variant id")
+        names = [a.name for a in self.arguments]
+        if len(set(names)) != len(names):
+            raise ValueError(f"{self.kernel_id}: duplicate argument name")
+        for arg in self.arguments:
+            _validate_source(self.kernel_id, arg.name, arg.source)
+        reserved = [i for i, a in enumerate(self.arguments) if a.source.get("kind") == "runtime_reserved"]
+        if reserved != [len(self.arguments) - 2, len(self.arguments) - 1]:
+            raise ValueError(f"{self.kernel_id}: two trailing runtime_reserved arguments are required")
+        if not 1 <= len(self.grid) <= 3:
+            raise ValueError(f"{self.kernel_id}: the grid needs one to three axes")
+        for axis in self.grid:
+            _validate_grid(self.kernel_id, axis, 0)
+        for v in self.variants:
+            for meta_name in _grid_meta_names(self.grid):
+                if meta_name not in v.meta:
+                    raise ValueError(f"{self.kernel_id}/{v.variant_id}: grid meta {meta_name} is missing")
+            if not 1 <= v.num_warps <= 32:
+                raise ValueError(f"{self.kernel_id}/{v.variant_id}: num_warps must be 1..32")
+            for override in v.arg_overrides:
+                if override not in names:
+                    raise ValueError(f"{self.kernel_id}/{v.variant_id}: override of unknown argument {override}")
+        for c in (*self.constraints, *(c for v in self.variants for c in v.constraints)):
+            kind = c.get("kind")
+            if kind not in _CONSTRAINT_FIELDS or set(c) - _CONSTRAINT_FIELDS[kind]:
+                raise ValueError(f"{self.kernel_id}: unsafe constraint {c}")
+            if "source" in c and c["source"] not in {"input", "output"}:
+                raise ValueError(f"{self.kernel_id}: invalid constraint source")
+
+
+def _validate_source(kernel_id: str, name: str, source: dict[str, Any]) -> None:
+    kind = source.get("kind")
+    if kind not in _SOURCE_FIELDS:
+        raise ValueError(f"{kernel_id}: unsafe source for {name}")
+    unknown = set(source) - _SOURCE_FIELDS[kind]
+    if unknown:
+        raise ValueError(f"{kernel_id}: unknown source field for {name}: {sorted(unknown)}")
+    if "prepack" in source and source["prepack"] not in _PREPACKS:
+        raise ValueError(f"{kernel_id}: unknown prepack transform for {name}")
+    if kind == "tensor_map":
+        if source.get("tensor") not in {"input", "output"}:
+            raise ValueError(f"{kernel_id}: tensor_map must name an input or output")
+        if source.get("swizzle", 0) not in {0, 32, 64, 128}:
+            raise ValueError(f"{kernel_id}: invalid tensor_map swizzle")
+
+
+def _validate_grid(kernel_id: str, node: dict[str, Any], depth: int) -> None:
+    if depth > 8:
+        raise ValueError(f"{kernel_id}: grid expression is too deep")
+    kind = node.get("kind")
+    if kind not in _GRID_FIELDS or set(node) - _GRID_FIELDS[kind]:
+        raise ValueError(f"{kernel_id}: unsafe grid expression {node}")
+    if kind in {"ceil_div", "mul"}:
+        if len(node.get("args", ())) != 2:
+            raise ValueError(f"{kernel_id}: {kind} needs two operands")
+        for arg in node["args"]:
+            _validate_grid(kernel_id, arg, depth + 1)
+
+
+def _grid_meta_names(grid: tuple[dict[str, Any], ...]) -> set[str]:
+    out: set[str] = set()
+
+    def walk(node: dict[str, Any]) -> None:
+        if node.get("kind") == "meta":
+            out.add(node["name"])
+        for arg in node.get("args", ()):
+            walk(arg)
+
+    for axis in grid:
+        walk(axis)
+    return out
+
+
+def _variant_arguments(spec: KernelSpec, variant: Variant) -> list[dict[str, Any]]:
+    out = []
+    for arg in spec.arguments:
+        source = dict(arg.source)
+        source.update(variant.arg_overrides.get(arg.name, {}))
+        out.append({"name": arg.name, "type": arg.type, "source": source})
+    return out
+
+
+def _padded_grid(grid: tuple[dict[str, Any], ...]) -> list[dict[str, Any]]:
+    axes = list(grid)
+    return axes + [{"kind": "literal", "value": 1} for _ in range(3 - len(axes))]
+
+
+def build_pack(output: Path, compile_cubin: Callable[[Path, Path, dict[str, str]], Path],
+               specs: list[KernelSpec] | None = None, jobs: int = 8) -> Path:
+    """Compiles every (spec, variant) to ``kernels/<id>/<variant>.cubin`` and
+    writes ``pack.json``. Unchanged cubins are not rebuilt."""
+    if specs is None:
+        from .kernel_specs import all_specs
+
+        specs = all_specs()
+    for spec in specs:
+        spec.validate()
+    output.mkdir(parents=True, exist_ok=True)
+    jobs_list = []
+    for spec in sorted(specs, key=lambda s: s.kernel_id):
+        for variant in spec.variants:
+            rel = Path("kernels") / spec.kernel_id / f"{variant.variant_id}.cubin"
+            jobs_list.append((spec, variant, rel))
+    with ThreadPoolExecutor(max_workers=jobs) as pool:
+        futures = [pool.submit(compile_cubin, KERNEL_DIR / spec.source, output / rel, dict(variant.defines))
+                   for spec, variant, rel in jobs_list]
+        for fut in futures:
+            fut.result()
+    entries = []
+    for spec, variant, rel in jobs_list:
+        digest = hashlib.sha256((output / rel).read_bytes()).hexdigest()
+        entries.append({
+            "kernel_id": spec.kernel_id,
+            "op_type": spec.op_type,
+            "kernel_version": spec.version,
+            "variant_id": variant.variant_id,
+            "default": variant.default,
+            "symbol": spec.symbol,
+            "binary": rel.as_posix(),
+            "binary_format": "cubin",
+            "sha256": digest,
+            "dtype": spec.dtype,
+            "layout": spec.layout,
+            "min_compute_capability": spec.min_compute_capability,
+            "num_warps": variant.num_warps,
+            "num_stages": 1,
+            "shared_memory_bytes": variant.shared_memory_bytes,
+            "arguments": _variant_arguments(spec, variant),
+            "grid": _padded_grid(spec.grid),
+            "constraints": [*spec.constraints, *variant.constraints],
+            "tuning": dict(variant.meta),
+        })
+    pack = {
+        "schema_version": PACK_SCHEMA_VERSION,
+        "abi_schema_version": ABI_SCHEMA_VERSION,
+        "pack_name": PACK_NAME,
+        "pack_version": PACK_VERSION,
+        "generator_version": GENERATOR_VERSION,
+        "triton_version": "none",
+        "kernels": entries,
+    }
+    # Remove cubins no longer named by any spec.
+    kernels_root = output / "kernels"
+    wanted = {str(rel) for _, _, rel in jobs_list}
+    if kernels_root.exists():
+        for path in kernels_root.rglob("*.cubin"):
+            if str(path.relative_to(output)) not in wanted:
+                path.unlink()
+    tmp = output / "pack.json.tmp"
+    tmp.write_text(json.dumps(pack, indent=2, sort_keys=True) + "\n", encoding="utf-8")
+    os.replace(tmp, output / "pack.json")
+    return output / "pack.json"

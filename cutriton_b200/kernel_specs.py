@@ -1,0 +1,264 @@
+"""Kernel descriptors of the sm_100a pack (consumed by :mod:`kernel_sdk`).
+
+Argument lists bind exactly the values the reference kernels bind
+(python/cutriton/triton_kernels/resnet.py:216-400, transformer.py:193-396),
+so graphs lower to the same op set; the kernels themselves are this
+package's CUDA sources under ``csrc/kernels``.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+from .kernel_sdk import Arg, KernelSpec, Variant
+
+
+def arg(arg_name: str, type_: str, kind: str, **source: Any) -> Arg:
+    return Arg(arg_name, type_, {"kind": kind, **source})
+
+
+RESERVED = (arg("runtime_scratch", "*i8", "runtime_reserved"), arg("profile_scratch", "*i8", "runtime_reserved"))
+
+
+def literal(value: int) -> dict[str, Any]:
+    return {"kind": "literal", "value": value}
+
+
+def meta(name: str) -> dict[str, Any]:
+    return {"kind": "meta", "name": name}
+
+
+def ceil_div(a: dict[str, Any], b: dict[str, Any]) -> dict[str, Any]:
+    return {"kind": "ceil_div", "args": [a, b]}
+
+
+def mul(a: dict[str, Any], b: dict[str, Any]) -> dict[str, Any]:
+    return {"kind": "mul", "args": [a, b]}
+
+
+def out_dim(axis: int, index: int = 0) -> dict[str, Any]:
+    return {"kind": "output_dim", "index": index, "axis": axis}
+
+
+def out_numel(index: int = 0) -> dict[str, Any]:
+    return {"kind": "output_numel", "index": index}
+
+
+CONV_DIMS = (
+    arg("n", "i32", "input_dim", index=0, axis=0),
+    arg("c", "i32", "input_dim", index=0, axis=1),
+    arg("h", "i32", "input_dim", index=0, axis=2),
+    arg("w", "i32", "input_dim", index=0, axis=3),
+    arg("k", "i32", "input_dim", index=1, axis=0),
+    arg("r", "i32", "input_dim", index=1, axis=2),
+    arg("s", "i32", "input_dim", index=1, axis=3),
+    arg("out_h", "i32", "output_dim", index=0, axis=2),
+    arg("out_w", "i32", "output_dim", index=0, axis=3),
+    arg("stride_h", "i32", "attribute_i64", name="strides", index=0, default=1),
+    arg("stride_w", "i32", "attribute_i64", name="strides", index=1, default=1),
+    arg("pad_h", "i32", "attribute_i64", name="pads", index=0, default=0),
+    arg("pad_w", "i32", "attribute_i64", name="pads", index=1, default=0),
+    arg("dilation_h", "i32", "attribute_i64", name="dilations", index=0, default=1),
+    arg("dilation_w", "i32", "attribute_i64", name="dilations", index=1, default=1),
+)
+BN_TENSORS = tuple(arg(n, "*fp32", "input", index=i + 2) for i, n in enumerate(("scale", "bias", "mean", "variance")))
+EPSILON = arg("epsilon", "fp32", "attribute_f64", name="batchnorm_epsilon", alternate_name="epsilon", default=1e-5)
+# Output pixels (n * oh * ow) tiled by BLOCK_M, channels by BLOCK_N.
+CONV_GRID = (
+    ceil_div(mul(out_dim(0), mul(out_dim(2), out_dim(3))), meta("BLOCK_M")),
+    ceil_div(out_dim(1), meta("BLOCK_N")),
+)
+SIMT_TILE = {"BLOCK_M": 64, "BLOCK_N": 64}
+
+
+def _conv_specs() -> list[KernelSpec]:
+    x_w = (arg("x", "*fp32", "input", index=0), arg("weight", "*fp32", "input", index=1))
+    out = (arg("output", "*fp32", "output", index=0),)
+    families = [
+        ("conv.fp32.nchw", "Conv", "ctb_conv_f32_simt", x_w + out + CONV_DIMS + RESERVED),
+        ("conv_bn.fp32.nchw", "FusedConvBatchNorm", "ctb_conv_bn_f32_simt",
+         x_w + BN_TENSORS + out + CONV_DIMS + (EPSILON,) + RESERVED),
+        ("conv_bn_relu.fp32.nchw", "FusedConvBatchNormRelu", "ctb_conv_bn_relu_f32_simt",
+         x_w + BN_TENSORS + out + CONV_DIMS + (EPSILON,) + RESERVED),
+        ("conv_bn_add_relu.fp32.nchw", "FusedConvBatchNormAddRelu", "ctb_conv_bn_add_relu_f32_simt",
+         x_w + BN_TENSORS + (arg("residual", "*fp32", "input", index=6),) + out + CONV_DIMS + (EPSILON,) + RESERVED),
+    ]
+    specs = []
+    for kernel_id, op_type, symbol, arguments in families:
+        specs.append(KernelSpec(
+            kernel_id=kernel_id, op_type=op_type, version=1, source="conv_simt.cu", symbol=symbol,
+            arguments=arguments, grid=CONV_GRID, layout="NCHW",
+            variants=(Variant("simt_m64n64", num_warps=8, meta=SIMT_TILE, default=True),),
+        ))
+    return specs
+
+
+def _elementwise_specs() -> list[KernelSpec]:
+    specs = []
+    chunk_f32 = {"CHUNK": 4096}
+    chunk_f16 = {"CHUNK": 8192}
+    grid = (ceil_div(out_numel(), meta("CHUNK")),)
+    for kernel_id, op_type, symbol, inputs, dtype, chunk, layout in (
+        ("relu.fp32", "Relu", "ctb_relu_f32", ("x",), "float32", chunk_f32, ""),
+        ("add.fp32", "Add", "ctb_add_f32", ("a", "b"), "float32", chunk_f32, ""),
+        ("add_relu.fp32", "AddRelu", "ctb_add_relu_f32", ("a", "b"), "float32", chunk_f32, ""),
+        ("gelu.fp16", "Gelu", "ctb_gelu_f16", ("x",), "float16", chunk_f16, ""),
+        ("add.fp16", "Add", "ctb_add_f16", ("a", "b"), "float16", chunk_f16, ""),
+    ):
+        ptr = "*fp32" if dtype == "float32" else "*fp16"
+        arguments = tuple(arg(n, ptr, "input", index=i) for i, n in enumerate(inputs)) + (
+            arg("output", ptr, "output", index=0),
+            arg("total", "i32", "output_numel", index=0),
+        ) + RESERVED
+        specs.append(KernelSpec(
+            kernel_id=kernel_id, op_type=op_type, version=1, source="elementwise.cu", symbol=symbol,
+            arguments=arguments, grid=grid, dtype=dtype, layout=layout,
+            variants=(Variant("vec16b", num_warps=8, meta=chunk, default=True),),
+        ))
+    bn_arguments = (
+        arg("x", "*fp32", "input", index=0),
+        arg("scale", "*fp32", "input", index=1),
+        arg("bias", "*fp32", "input", index=2),
+        arg("mean", "*fp32", "input", index=3),
+        arg("variance", "*fp32", "input", index=4),
+        arg("output", "*fp32", "output", index=0),
+        arg("total", "i32", "output_numel", index=0),
+        arg("channels", "i32", "input_dim", index=0, axis=1),
+        arg("spatial", "i32", "input_dim_product", index=0, begin_axis=2),
+        arg("epsilon", "fp32", "attribute_f64", name="epsilon", alternate_name="batchnorm_epsilon", default=1e-5),
+    ) + RESERVED
+    specs.append(KernelSpec(
+        kernel_id="batch_norm.fp32.nchw", op_type="BatchNormalization", version=1, source="elementwise.cu",
+        symbol="ctb_batch_norm_f32", arguments=bn_arguments, grid=grid, layout="NCHW",
+        variants=(Variant("vec16b", num_warps=8, meta=chunk_f32, default=True),),
+    ))
+    return specs
+
+
+def _pool_specs() -> list[KernelSpec]:
+    pool_arguments = (
+        arg("x", "*fp32", "input", index=0),
+        arg("output", "*fp32", "output", index=0),
+        arg("n", "i32", "input_dim", index=0, axis=0),
+        arg("c", "i32", "input_dim", index=0, axis=1),
+        arg("h", "i32", "input_dim", index=0, axis=2),
+        arg("w", "i32", "input_dim", index=0, axis=3),
+        arg("out_h", "i32", "output_dim", index=0, axis=2),
+        arg("out_w", "i32", "output_dim", index=0, axis=3),
+        arg("kernel_h", "i32", "attribute_i64", name="kernel_shape", index=0, default=1),
+        arg("kernel_w", "i32", "attribute_i64", name="kernel_shape", index=1, default=1),
+        arg("stride_h", "i32", "attribute_i64", name="strides", index=0, default=1),
+        arg("stride_w", "i32", "attribute_i64", name="strides", index=1, default=1),
+        arg("pad_h", "i32", "attribute_i64", name="pads", index=0, default=0),
+        arg("pad_w", "i32", "attribute_i64", name="pads", index=1, default=0),
+        arg("dilation_h", "i32", "attribute_i64", name="dilations", index=0, default=1),
+        arg("dilation_w", "i32", "attribute_i64", name="dilations", index=1, default=1),
+    ) + RESERVED
+    gap_arguments = (
+        arg("x", "*fp32", "input", index=0),
+        arg("output", "*fp32", "output", index=0),
+        arg("n", "i32", "input_dim", index=0, axis=0),
+        arg("c", "i32", "input_dim", index=0, axis=1),
+        arg("h", "i32", "input_dim", index=0, axis=2),
+        arg("w", "i32", "input_dim", index=0, axis=3),
+    ) + RESERVED
+    return [
+        KernelSpec(
+            kernel_id="max_pool.fp32.nchw", op_type="MaxPool", version=1, source="pool.cu",
+            symbol="ctb_max_pool_f32", arguments=pool_arguments, layout="NCHW",
+            grid=(ceil_div(out_numel(), meta("BLOCK")),),
+            variants=(Variant("thread_per_output", num_warps=8, meta={"BLOCK": 256}, default=True),),
+        ),
+        KernelSpec(
+            kernel_id="global_average_pool.fp32.nchw", op_type="GlobalAveragePool", version=1, source="pool.cu",
+            symbol="ctb_global_average_pool_f32", arguments=gap_arguments, layout="NCHW",
+            grid=(ceil_div(out_numel(), meta("PLANES")),),
+            variants=(Variant("warp_per_plane", num_warps=8, meta={"PLANES": 8}, default=True),),
+        ),
+    ]
+
+
+GEMM_CONSTRAINTS = (
+    {"kind": "input_count_eq", "value": 2},
+    {"kind": "attribute_i64_eq", "name": "transA", "value": 0, "default": 0},
+    {"kind": "attribute_i64_eq", "name": "transB", "value": 0, "default": 0},
+    {"kind": "tensor_rank_eq", "source": "input", "index": 0, "value": 2},
+    {"kind": "tensor_rank_eq", "source": "input", "index": 1, "value": 2},
+)
+
+
+def _gemm_specs() -> list[KernelSpec]:
+    def gemm_args(ptr: str) -> tuple[Arg, ...]:
+        return (
+            arg("a", ptr, "input", index=0),
+            arg("b", ptr, "input", index=1),
+            arg("output", ptr, "output", index=0),
+            arg("m", "i32", "output_dim", index=0, axis=0),
+            arg("n", "i32", "output_dim", index=0, axis=1),
+            arg("k", "i32", "input_dim", index=0, axis=1),
+        ) + RESERVED
+
+    grid = (ceil_div(out_dim(0), meta("BLOCK_M")), ceil_div(out_dim(1), meta("BLOCK_N")))
+    return [
+        KernelSpec(
+            kernel_id="gemm.fp32", op_type="Gemm", version=1, source="conv_simt.cu", symbol="ctb_gemm_f32_simt",
+            arguments=gemm_args("*fp32"), grid=grid, constraints=GEMM_CONSTRAINTS,
+            variants=(Variant("simt_m64n64", num_warps=8, meta=SIMT_TILE, default=True),),
+        ),
+        KernelSpec(
+            kernel_id="gemm.fp16.wmma", op_type="Gemm", version=1, source="gemm_f16_wmma.cu",
+            symbol="ctb_gemm_f16_wmma", arguments=gemm_args("*fp16"), grid=grid, dtype="float16",
+            constraints=GEMM_CONSTRAINTS,
+            variants=(Variant("m128n128k32", num_warps=8, meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=True),),
+        ),
+        KernelSpec(
+            kernel_id="gemm_gelu.fp16.wmma", op_type="GemmGelu", version=1, source="gemm_f16_wmma.cu",
+            symbol="ctb_gemm_gelu_f16_wmma", arguments=gemm_args("*fp16"), grid=grid, dtype="float16",
+            constraints=GEMM_CONSTRAINTS,
+            variants=(Variant("m128n128k32", num_warps=8, meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=True),),
+        ),
+    ]
+
+
+def _norm_specs() -> list[KernelSpec]:
+    def norm_args(skip: bool) -> tuple[Arg, ...]:
+        names = ("x", "residual", "scale", "bias") if skip else ("x", "scale", "bias")
+        return tuple(arg(n, "*fp16", "input", index=i) for i, n in enumerate(names)) + (
+            arg("output", "*fp16", "output", index=0),
+            arg("rows", "i32", "input_dim", index=0, axis=0),
+            arg("columns", "i32", "input_dim", index=0, axis=1),
+            arg("epsilon", "fp32", "attribute_f64", name="epsilon", default=1e-5),
+        ) + RESERVED
+
+    def row_constraints(inputs: int | None) -> tuple[dict[str, Any], ...]:
+        out: tuple[dict[str, Any], ...] = (
+            {"kind": "tensor_rank_eq", "source": "input", "index": 0, "value": 2},
+            {"kind": "dim_le", "source": "input", "index": 0, "axis": 1, "value": 1024},
+        )
+        if inputs is not None:
+            out = ({"kind": "input_count_eq", "value": inputs},) + out
+        return out
+
+    grid = (ceil_div(out_dim(0), meta("ROWS")),)
+    softmax_args = (
+        arg("x", "*fp16", "input", index=0),
+        arg("output", "*fp16", "output", index=0),
+        arg("rows", "i32", "input_dim", index=0, axis=0),
+        arg("columns", "i32", "input_dim", index=0, axis=1),
+    ) + RESERVED
+    variants = (Variant("warp_per_row", num_warps=8, meta={"ROWS": 8}, default=True),)
+    return [
+        KernelSpec(kernel_id="layer_norm.fp16.last_axis", op_type="LayerNormalization", version=1,
+                   source="norm.cu", symbol="ctb_layer_norm_f16", arguments=norm_args(False), grid=grid,
+                   dtype="float16", constraints=row_constraints(3), variants=variants),
+        KernelSpec(kernel_id="skip_layer_norm.fp16.last_axis", op_type="SkipLayerNormalization", version=1,
+                   source="norm.cu", symbol="ctb_skip_layer_norm_f16", arguments=norm_args(True), grid=grid,
+                   dtype="float16", constraints=row_constraints(4), variants=variants),
+        KernelSpec(kernel_id="softmax.fp16.last_axis", op_type="Softmax", version=1, source="norm.cu",
+                   symbol="ctb_softmax_f16", arguments=softmax_args, grid=grid, dtype="float16",
+                   constraints=row_constraints(None), variants=variants),
+    ]
+
+
+def all_specs() -> list[KernelSpec]:
+    return [*_conv_specs(), *_elementwise_specs(), *_pool_specs(), *_gemm_specs(), *_norm_specs()]

@@ -1,0 +1,150 @@
+"""Kernel Pack loader and SDK: schema/ABI/SHA/SM/grid validation (negative
+cases of the reference's tests/cpp/test_cuda.cpp:488-552 and
+tests/python/test_kernel_sdk.py:45-107), exercised without a GPU."""
+
+from __future__ import annotations
+
+import json
+import shutil
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import cutriton_b200 as ct
+from cutriton_b200 import kernel_sdk, kernel_specs
+
+
+@pytest.fixture()
+def relu_model():
+    model = ct.Model()
+    model.add_input("x", [1, 4, 5, 5])
+    model.add_node("relu", "Relu", ["x"], ["y"])
+    model.add_output("y")
+    return model
+
+
+@pytest.fixture()
+def assume_sm100(monkeypatch):
+    monkeypatch.setenv("CUTRITON_ASSUME_COMPUTE_CAPABILITY", "100")
+
+
+def copy_pack(tmp_path: Path) -> Path:
+    dst = tmp_path / "pack"
+    shutil.copytree(ct.PACK_DIR, dst, ignore=shutil.ignore_patterns("tuning"))
+    return dst
+
+
+def test_builtin_pack_compiles_graph(relu_model, assume_sm100):
+    engine = ct.build_engine(relu_model)
+    ops = engine.ops()
+    assert [o["op_type"] for o in ops] == ["Relu"]
+    assert ops[0]["candidates"][ops[0]["default"]].startswith("cutriton_sm100:relu.fp32")
+
+
+def test_missing_pack_is_not_found(relu_model, assume_sm100, tmp_path):
+    with pytest.raises(ct.CutritonError) as err:
+        ct.build_engine(relu_model, kernel_artifact_dir=str(tmp_path / "missing"))
+    assert err.value.code == ct.NOT_FOUND
+
+
+def test_schema_v1_is_rejected(relu_model, assume_sm100, tmp_path):
+    pack = copy_pack(tmp_path)
+    doc = json.loads((pack / "pack.json").read_text())
+    doc["schema_version"] = 1
+    (pack / "pack.json").write_text(json.dumps(doc))
+    with pytest.raises(ct.CutritonError) as err:
+        ct.build_engine(relu_model, kernel_artifact_dir=str(pack))
+    assert err.value.code == ct.INVALID_ARGUMENT
+
+
+def test_sha_mismatch_is_rejected(relu_model, assume_sm100, tmp_path):
+    pack = copy_pack(tmp_path)
+    cubin = next((pack / "kernels").rglob("*.cubin"))
+    with open(cubin, "ab") as f:
+        f.write(b"\0")
+    with pytest.raises(ct.CutritonError) as err:
+        ct.build_engine(relu_model, kernel_artifact_dir=str(pack))
+    assert err.value.code == ct.INVALID_ARGUMENT
+    assert "SHA-256" in str(err.value)
+
+
+def test_sm_mismatch_is_unsupported(relu_model, assume_sm100, tmp_path):
+    pack = copy_pack(tmp_path)
+    doc = json.loads((pack / "pack.json").read_text())
+    for k in doc["kernels"]:
+        k["min_compute_capability"] = 999
+    (pack / "pack.json").write_text(json.dumps(doc))
+    with pytest.raises(ct.CutritonError) as err:
+        ct.build_engine(relu_model, kernel_artifact_dir=str(pack))
+    assert err.value.code == ct.UNSUPPORTED
+
+
+@pytest.mark.parametrize("mutation", [
+    lambda k: k.__setitem__("grid", [{"kind": "python", "expression": "unsafe"}]),
+    lambda k: k["arguments"].pop(),                                  # reserved tail broken
+    lambda k: k.__setitem__("binary", "../escape.cubin"),
+    lambda k: k["constraints"].append({"kind": "lambda", "value": 1}),
+    lambda k: k["arguments"][0]["source"].__setitem__("kind", "eval"),
+    lambda k: k.__setitem__("binary_format", "elf"),
+])
+def test_unsafe_manifest_entries_are_rejected(relu_model, assume_sm100, tmp_path, mutation):
+    pack = copy_pack(tmp_path)
+    doc = json.loads((pack / "pack.json").read_text())
+    mutation(doc["kernels"][0])
+    (pack / "pack.json").write_text(json.dumps(doc))
+    with pytest.raises(ct.CutritonError) as err:
+        ct.build_engine(relu_model, kernel_artifact_dir=str(pack))
+    assert err.value.code == ct.INVALID_ARGUMENT
+
+
+def test_abi_v1_grid_is_accepted(relu_model, assume_sm100, tmp_path):
+    pack = copy_pack(tmp_path)
+    doc = json.loads((pack / "pack.json").read_text())
+    doc["abi_schema_version"] = 1
+    for k in doc["kernels"]:
+        k["grid"] = {"op": "ceil_div", "value": {"kind": "output_numel", "index": 0}, "divisor": 4096}
+    (pack / "pack.json").write_text(json.dumps(doc))
+    engine = ct.build_engine(relu_model, kernel_artifact_dir=str(pack))
+    assert engine.num_ops() == 1
+
+
+def test_sdk_validates_specs():
+    specs = kernel_specs.all_specs()
+    for spec in specs:
+        spec.validate()
+    base = next(s for s in specs if s.kernel_id == "relu.fp32")
+
+    def variant(**kw):
+        return kernel_sdk.Variant(**{"variant_id": "v", "num_warps": 8, "meta": {"CHUNK": 4096}, "default": True, **kw})
+
+    bad = [
+        kernel_sdk.KernelSpec(**{**base.__dict__, "variants": (variant(default=False),)}),
+        kernel_sdk.KernelSpec(**{**base.__dict__, "variants": (variant(), variant())}),
+        kernel_sdk.KernelSpec(**{**base.__dict__, "arguments": base.arguments[:-1]}),
+        kernel_sdk.KernelSpec(**{**base.__dict__, "arguments": (kernel_sdk.Arg("x", "*fp32", {"kind": "eval"}),)
+                                 + base.arguments[1:]}),
+        kernel_sdk.KernelSpec(**{**base.__dict__, "grid": ({"kind": "python"},)}),
+        kernel_sdk.KernelSpec(**{**base.__dict__, "variants": (variant(meta={}),)}),
+        kernel_sdk.KernelSpec(**{**base.__dict__, "constraints": ({"kind": "lambda"},)}),
+        kernel_sdk.KernelSpec(**{**base.__dict__, "arguments": (kernel_sdk.Arg(
+            "x", "*fp32", {"kind": "input", "index": 0, "prepack": "unknown"}),) + base.arguments[1:]}),
+    ]
+    for spec in bad:
+        with pytest.raises(ValueError):
+            spec.validate()
+
+
+def test_pack_entries_are_cubins_for_sm100():
+    doc = json.loads((ct.PACK_DIR / "pack.json").read_text())
+    assert doc["schema_version"] == 2 and doc["abi_schema_version"] == 2
+    for k in doc["kernels"]:
+        assert k["binary_format"] == "cubin"
+        assert k["min_compute_capability"] == 100
+        data = (ct.PACK_DIR / k["binary"]).read_bytes()
+        assert data[:4] == b"\x7fELF"
+    op_defaults = {}
+    for k in doc["kernels"]:
+        op_defaults.setdefault((k["op_type"], k["dtype"]), []).append(k["default"])
+    for key, flags in op_defaults.items():
+        assert sum(flags) == 1, key
