@@ -104,8 +104,8 @@ class KernelSpec:
     def validate(self) -> None:
         if not self.kernel_id or not self.op_type or self.version <= 0 or not self.symbol:
             raise ValueError("KernelSpec identity is incomplete")
-        if not self.variants or sum(v.default for v in self.variants) != 1:
-            raise ValueError(f"{self.kernel_id}: exactly one default variant is required")
+        if not self.variants or sum(v.default for v in self.variants) > 1:
+            raise ValueError(f"{self.kernel_id}: at most one default variant is allowed")
         if len({v.variant_id for v in self.variants}) != len(self.variants):
             raise ValueError(f"{self.kernel_id}: duplicate variant id")
         names = [a.name for a in self.arguments]
@@ -135,6 +135,20 @@ class KernelSpec:
                 raise ValueError(f"{self.kernel_id}: unsafe constraint {c}")
             if "source" in c and c["source"] not in {"input", "output"}:
                 raise ValueError(f"{self.kernel_id}: invalid constraint source")
+
+
+def validate_pack(specs: list[KernelSpec]) -> None:
+    """Validates every spec and requires exactly one default variant per
+    (op_type, dtype) across the pack — the kernel lowering falls back to
+    (reference src/backend/backend.cpp:207-218)."""
+    defaults: dict[tuple[str, str], int] = {}
+    for spec in specs:
+        spec.validate()
+        key = (spec.op_type, spec.dtype)
+        defaults[key] = defaults.get(key, 0) + sum(v.default for v in spec.variants)
+    for key, count in defaults.items():
+        if count != 1:
+            raise ValueError(f"{key[0]}/{key[1]}: exactly one default variant is required, found {count}")
 
 
 def _validate_source(kernel_id: str, name: str, source: dict[str, Any]) -> None:
@@ -202,8 +216,7 @@ def build_pack(output: Path, compile_cubin: Callable[[Path, Path, dict[str, str]
         from .kernel_specs import all_specs
 
         specs = all_specs()
-    for spec in specs:
-        spec.validate()
+    validate_pack(specs)
     output.mkdir(parents=True, exist_ok=True)
     jobs_list = []
     for spec in sorted(specs, key=lambda s: s.kernel_id):

@@ -199,7 +199,43 @@ def _gemm_specs() -> list[KernelSpec]:
         ) + RESERVED
 
     grid = (ceil_div(out_dim(0), meta("BLOCK_M")), ceil_div(out_dim(1), meta("BLOCK_N")))
-    return [
+
+    def tc_args(block_n: int) -> tuple[Arg, ...]:
+        return (
+            arg("tma_a", "tensormap", "tensor_map", tensor="input", index=0, box=[64, 128], swizzle=128),
+            arg("tma_b", "tensormap", "tensor_map", tensor="input", index=1, box=[64, block_n], swizzle=128,
+                prepack="transpose_2d"),
+            arg("output", "*fp16", "output", index=0),
+            arg("m", "i32", "output_dim", index=0, axis=0),
+            arg("n", "i32", "output_dim", index=0, axis=1),
+            arg("k", "i32", "input_dim", index=0, axis=1),
+        ) + RESERVED
+
+    tc_constraints = GEMM_CONSTRAINTS + (
+        {"kind": "input_is_constant", "index": 1},
+        {"kind": "dim_multiple_of", "source": "input", "index": 0, "axis": 1, "value": 8},
+        {"kind": "dim_multiple_of", "source": "output", "index": 0, "axis": 1, "value": 8},
+    )
+
+    def tc_variants() -> tuple[Variant, ...]:
+        out = []
+        for block_n, stages, default in ((128, 4, True), (128, 3, False), (256, 3, False)):
+            smem = stages * (128 * 64 * 2 + block_n * 64 * 2) + 1024 + 256
+            out.append(Variant(f"m128n{block_n}k64s{stages}", num_warps=4, shared_memory_bytes=smem,
+                               meta={"BLOCK_M": 128, "BLOCK_N": block_n},
+                               defines={"CTB_BLOCK_N": str(block_n), "CTB_STAGES": str(stages)}, default=default,
+                               arg_overrides={"tma_b": {"box": [64, block_n]}}))
+        return tuple(out)
+
+    tc = [
+        KernelSpec(kernel_id="gemm.fp16.tcgen05", op_type="Gemm", version=1, source="gemm_f16_tc.cu",
+                   symbol="ctb_gemm_f16_tc", arguments=tc_args(128), grid=grid, dtype="float16",
+                   constraints=tc_constraints, variants=tc_variants()),
+        KernelSpec(kernel_id="gemm_gelu.fp16.tcgen05", op_type="GemmGelu", version=1, source="gemm_f16_tc.cu",
+                   symbol="ctb_gemm_gelu_f16_tc", arguments=tc_args(128), grid=grid, dtype="float16",
+                   constraints=tc_constraints, variants=tc_variants()),
+    ]
+    return tc + [
         KernelSpec(
             kernel_id="gemm.fp32", op_type="Gemm", version=1, source="conv_simt.cu", symbol="ctb_gemm_f32_simt",
             arguments=gemm_args("*fp32"), grid=grid, constraints=GEMM_CONSTRAINTS,
@@ -209,13 +245,13 @@ def _gemm_specs() -> list[KernelSpec]:
             kernel_id="gemm.fp16.wmma", op_type="Gemm", version=1, source="gemm_f16_wmma.cu",
             symbol="ctb_gemm_f16_wmma", arguments=gemm_args("*fp16"), grid=grid, dtype="float16",
             constraints=GEMM_CONSTRAINTS,
-            variants=(Variant("m128n128k32", num_warps=8, meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=True),),
+            variants=(Variant("m128n128k32", num_warps=8, meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=False),),
         ),
         KernelSpec(
             kernel_id="gemm_gelu.fp16.wmma", op_type="GemmGelu", version=1, source="gemm_f16_wmma.cu",
             symbol="ctb_gemm_gelu_f16_wmma", arguments=gemm_args("*fp16"), grid=grid, dtype="float16",
             constraints=GEMM_CONSTRAINTS,
-            variants=(Variant("m128n128k32", num_warps=8, meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=True),),
+            variants=(Variant("m128n128k32", num_warps=8, meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=False),),
         ),
     ]
 

@@ -118,8 +118,10 @@ def test_sdk_validates_specs():
     def variant(**kw):
         return kernel_sdk.Variant(**{"variant_id": "v", "num_warps": 8, "meta": {"CHUNK": 4096}, "default": True, **kw})
 
+    with pytest.raises(ValueError):  # an op without a default variant
+        kernel_sdk.validate_pack([kernel_sdk.KernelSpec(**{**base.__dict__, "variants": (variant(default=False),)})])
+    kernel_sdk.validate_pack(specs)
     bad = [
-        kernel_sdk.KernelSpec(**{**base.__dict__, "variants": (variant(default=False),)}),
         kernel_sdk.KernelSpec(**{**base.__dict__, "variants": (variant(), variant())}),
         kernel_sdk.KernelSpec(**{**base.__dict__, "arguments": base.arguments[:-1]}),
         kernel_sdk.KernelSpec(**{**base.__dict__, "arguments": (kernel_sdk.Arg("x", "*fp32", {"kind": "eval"}),)
