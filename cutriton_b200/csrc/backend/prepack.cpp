@@ -41,17 +41,21 @@ inline void SplitTf32(float x, float* hi, float* lo) {
   *lo = x - *hi;
 }
 
-// OIHW fp32 weights -> [2][O][R][S][I] (hi plane, then lo plane): the
-// implicit-GEMM B operand, K-major with K ordered (r, s, c) so a K-block of
-// channels at one filter tap is contiguous.
+// OIHW fp32 weights -> [2][O][Kpad] (hi plane, then lo plane), the
+// implicit-GEMM A operand of the tensor-core convolution: K-major with
+// k = (r * S + s) * I + i (channels fastest, so a 32-wide k block is one
+// filter tap of 32 channels when I % 32 == 0), zero-padded to a multiple of
+// 32 so every k block is a whole 128-byte TMA row.
 Status ConvWeightSplit(const TensorDesc& in, const void* data, TensorDesc* out,
                        std::vector<std::uint8_t>* bytes) {
   if (in.shape.size() != 4 || in.dtype != DataType::kFloat32) {
-    return Status::ShapeError("conv_w_tf32x2_orsi expects an OIHW float32 constant");
+    return Status::ShapeError("conv_w_tf32x2_okpad expects an OIHW float32 constant");
   }
   const int64_t O = in.shape[0], I = in.shape[1], R = in.shape[2], S = in.shape[3];
-  const std::size_t plane = static_cast<std::size_t>(O * R * S * I);
-  *out = TensorDesc({2, O, R, S, I}, DataType::kFloat32, in.device_type, in.device_id, "");
+  const int64_t K = I * R * S;
+  const int64_t Kpad = (K + 31) / 32 * 32;
+  const std::size_t plane = static_cast<std::size_t>(O * Kpad);
+  *out = TensorDesc({2, O, Kpad}, DataType::kFloat32, in.device_type, in.device_id, "");
   bytes->assign(2 * plane * sizeof(float), 0);
   const auto* w = static_cast<const float*>(data);
   auto* dst = reinterpret_cast<float*>(bytes->data());
@@ -61,7 +65,7 @@ Status ConvWeightSplit(const TensorDesc& in, const void* data, TensorDesc* out,
         for (int64_t s = 0; s < S; ++s) {
           float hi, lo;
           SplitTf32(w[((o * I + i) * R + r) * S + s], &hi, &lo);
-          const std::size_t at = static_cast<std::size_t>(((o * R + r) * S + s) * I + i);
+          const std::size_t at = static_cast<std::size_t>(o * Kpad + (r * S + s) * I + i);
           dst[at] = hi;
           dst[plane + at] = lo;
         }
@@ -93,7 +97,7 @@ Status GemmWeightSplit(const TensorDesc& in, const void* data, TensorDesc* out,
 const std::unordered_map<std::string, Transform>& Registry() {
   static const std::unordered_map<std::string, Transform> table = {
       {"transpose_2d", Transpose2d},
-      {"conv_w_tf32x2_orsi", ConvWeightSplit},
+      {"conv_w_tf32x2_okpad", ConvWeightSplit},
       {"gemm_w_tf32x2_nk", GemmWeightSplit},
   };
   return table;

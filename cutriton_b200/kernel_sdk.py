@@ -63,7 +63,7 @@ _GRID_FIELDS = {
     "ceil_div": {"kind", "args"},
     "mul": {"kind", "args"},
 }
-_PREPACKS = {"transpose_2d", "conv_w_tf32x2_orsi", "gemm_w_tf32x2_nk"}
+_PREPACKS = {"transpose_2d", "conv_w_tf32x2_okpad", "gemm_w_tf32x2_nk"}
 
 
 @dataclass(frozen=True)

@@ -88,7 +88,36 @@ def _conv_specs() -> list[KernelSpec]:
         specs.append(KernelSpec(
             kernel_id=kernel_id, op_type=op_type, version=1, source="conv_simt.cu", symbol=symbol,
             arguments=arguments, grid=CONV_GRID, layout="NCHW",
-            variants=(Variant("simt_m64n64", num_warps=8, meta=SIMT_TILE, default=True),),
+            variants=(Variant("simt_m64n64", num_warps=8, meta=SIMT_TILE, default=False),),
+        ))
+    # 3xTF32 tcgen05 implicit GEMM: output channels on M, output pixels on N.
+    tma_w = arg("tma_w", "tensormap", "tensor_map", tensor="input", index=1, box=[32, 128, 1], swizzle=128,
+                prepack="conv_w_tf32x2_okpad")
+    x = (arg("x", "*fp32", "input", index=0),)
+    tc_families = [
+        ("conv.fp32.nchw.tcgen05", "Conv", "ctb_conv_f32_tc", (tma_w,) + x + out + CONV_DIMS + RESERVED),
+        ("conv_bn.fp32.nchw.tcgen05", "FusedConvBatchNorm", "ctb_conv_bn_f32_tc",
+         (tma_w,) + x + BN_TENSORS + out + CONV_DIMS + (EPSILON,) + RESERVED),
+        ("conv_bn_relu.fp32.nchw.tcgen05", "FusedConvBatchNormRelu", "ctb_conv_bn_relu_f32_tc",
+         (tma_w,) + x + BN_TENSORS + out + CONV_DIMS + (EPSILON,) + RESERVED),
+        ("conv_bn_add_relu.fp32.nchw.tcgen05", "FusedConvBatchNormAddRelu", "ctb_conv_bn_add_relu_f32_tc",
+         (tma_w,) + x + BN_TENSORS + (arg("residual", "*fp32", "input", index=6),) + out + CONV_DIMS
+         + (EPSILON,) + RESERVED),
+    ]
+    tc_grid = (
+        ceil_div(mul(out_dim(0), mul(out_dim(2), out_dim(3))), meta("BLOCK_PIXELS")),
+        ceil_div(out_dim(1), meta("BLOCK_CHANNELS")),
+    )
+    for kernel_id, op_type, symbol, arguments in tc_families:
+        stages = 3
+        specs.append(KernelSpec(
+            kernel_id=kernel_id, op_type=op_type, version=1, source="conv_tc.cu", symbol=symbol,
+            arguments=arguments, grid=tc_grid, layout="NCHW",
+            constraints=({"kind": "input_is_constant", "index": 1},),
+            variants=(Variant(f"m128n128k32s{stages}_3xtf32", num_warps=8,
+                              shared_memory_bytes=stages * 65536 + 1024 + 256,
+                              meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128},
+                              defines={"CTB_STAGES": str(stages)}, default=True),),
         ))
     return specs
 
