@@ -273,7 +273,7 @@ Status BindArguments(const KernelInvocation& inv, KernelContext* context, BoundP
   return Status::OK();
 }
 
-Status EvaluateGrid(const GridExpression& e, const KernelInvocation& inv, KernelContext* context,
+Status EvaluateGrid(const GridExpression& e, const KernelInvocation& inv, KernelContext* context, int sm_count,
                     int64_t* value) {
   auto tensor_of = [&](bool output, int index, const Tensor** t) -> Status {
     const auto& names = output ? inv.outputs : inv.inputs;
@@ -311,15 +311,21 @@ Status EvaluateGrid(const GridExpression& e, const KernelInvocation& inv, Kernel
       CUTRITON_RETURN_IF_ERROR(tensor_of(e.kind == GridExpressionKind::kOutputNumElements, e.tensor_index, &t));
       *value = t->desc().NumElements();
       break;
+    case GridExpressionKind::kDeviceSmCount:
+      *value = sm_count;
+      break;
     case GridExpressionKind::kCeilDiv:
-    case GridExpressionKind::kMultiply: {
+    case GridExpressionKind::kMultiply:
+    case GridExpressionKind::kMinimum: {
       if (e.operands.size() != 2) return Status::InvalidArgument("launch-grid binary expression is malformed");
       int64_t lhs = 0, rhs = 0;
-      CUTRITON_RETURN_IF_ERROR(EvaluateGrid(e.operands[0], inv, context, &lhs));
-      CUTRITON_RETURN_IF_ERROR(EvaluateGrid(e.operands[1], inv, context, &rhs));
+      CUTRITON_RETURN_IF_ERROR(EvaluateGrid(e.operands[0], inv, context, sm_count, &lhs));
+      CUTRITON_RETURN_IF_ERROR(EvaluateGrid(e.operands[1], inv, context, sm_count, &rhs));
       if (lhs <= 0 || rhs <= 0) return Status::ShapeError("launch-grid operands must be positive");
       if (e.kind == GridExpressionKind::kCeilDiv) {
         *value = (lhs + rhs - 1) / rhs;
+      } else if (e.kind == GridExpressionKind::kMinimum) {
+        *value = lhs < rhs ? lhs : rhs;
       } else {
         if (lhs > std::numeric_limits<int64_t>::max() / rhs) {
           return Status::ShapeError("launch-grid multiplication overflows");
@@ -334,8 +340,9 @@ Status EvaluateGrid(const GridExpression& e, const KernelInvocation& inv, Kernel
 
 class InvocationKernel final : public OpKernel {
  public:
-  InvocationKernel(KernelInvocation invocation, std::shared_ptr<CudaModuleCache> cache, CUfunction fn)
-      : invocation_(std::move(invocation)), cache_(std::move(cache)), function_(fn) {}
+  InvocationKernel(KernelInvocation invocation, std::shared_ptr<CudaModuleCache> cache, CUfunction fn,
+                   int sm_count)
+      : invocation_(std::move(invocation)), cache_(std::move(cache)), function_(fn), sm_count_(sm_count) {}
 
   const char* backend_name() const override { return "cuda_sm100"; }
   const char* op_type() const override { return invocation_.artifact.op_type.c_str(); }
@@ -348,7 +355,8 @@ class InvocationKernel final : public OpKernel {
     unsigned int grid[3] = {1, 1, 1};
     for (int axis = 0; axis < 3; ++axis) {
       int64_t extent = 0;
-      CUTRITON_RETURN_IF_ERROR(EvaluateGrid(invocation_.artifact.launch_grid[axis], invocation_, context, &extent));
+      CUTRITON_RETURN_IF_ERROR(
+          EvaluateGrid(invocation_.artifact.launch_grid[axis], invocation_, context, sm_count_, &extent));
       const int64_t limit = axis == 0 ? 2147483647LL : 65535LL;
       if (extent > limit) return Status::ShapeError("launch-grid dimension exceeds CUDA limits");
       grid[axis] = static_cast<unsigned int>(extent);
@@ -366,6 +374,7 @@ class InvocationKernel final : public OpKernel {
   KernelInvocation invocation_;
   std::shared_ptr<CudaModuleCache> cache_;
   CUfunction function_{};
+  int sm_count_{1};
   BoundParameters params_;
 };
 
@@ -382,11 +391,16 @@ Status CreateCudaModuleCache(int device_id, std::shared_ptr<CudaModuleCache>* ca
 Status CreateInvocationKernel(const KernelInvocation& invocation, int device_id,
                               std::shared_ptr<CudaModuleCache> cache,
                               std::unique_ptr<OpKernel>* kernel) {
-  (void)device_id;
   if (kernel == nullptr || cache == nullptr) return Status::InvalidArgument("invocation kernel arguments are invalid");
   CUfunction function{};
   CUTRITON_RETURN_IF_ERROR(cache->GetFunction(invocation.artifact, &function));
-  *kernel = std::make_unique<InvocationKernel>(invocation, std::move(cache), function);
+  CUdevice device{};
+  int sm_count = 0;
+  const auto& api = drv::Get();
+  CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuDeviceGet(&device, device_id), "cuDeviceGet"));
+  CUTRITON_RETURN_IF_ERROR(drv::Check(
+      api.cuDeviceGetAttribute(&sm_count, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT, device), "cuDeviceGetAttribute"));
+  *kernel = std::make_unique<InvocationKernel>(invocation, std::move(cache), function, sm_count);
   return Status::OK();
 }
 

@@ -138,11 +138,16 @@ GridExpression GridNode(const json::Value& v, int depth) {
     e.kind = GridExpressionKind::kVariantMeta;
     e.meta_name = v.at("name").str();
     if (e.meta_name.empty()) throw std::runtime_error("grid meta name is empty");
-  } else if (kind == "ceil_div" || kind == "mul") {
+  } else if (kind == "sm_count") {
+    OnlyKeys(v, {"kind"}, "grid expression");
+    e.kind = GridExpressionKind::kDeviceSmCount;
+  } else if (kind == "ceil_div" || kind == "mul" || kind == "min") {
     OnlyKeys(v, {"kind", "args"}, "grid expression");
     const auto& args = v.at("args").list();
     if (args.size() != 2) throw std::runtime_error(kind + " grid expression needs two operands");
-    e.kind = kind == "ceil_div" ? GridExpressionKind::kCeilDiv : GridExpressionKind::kMultiply;
+    e.kind = kind == "ceil_div" ? GridExpressionKind::kCeilDiv
+             : kind == "mul"    ? GridExpressionKind::kMultiply
+                                : GridExpressionKind::kMinimum;
     for (const auto& arg : args) e.operands.push_back(GridNode(arg, depth + 1));
   } else {
     throw std::runtime_error("unsupported grid expression kind: " + kind);

@@ -43,16 +43,19 @@ inline void SplitTf32(float x, float* hi, float* lo) {
 
 // OIHW fp32 weights -> [2][O][Kpad] (hi plane, then lo plane), the
 // implicit-GEMM A operand of the tensor-core convolution: K-major with
-// k = (r * S + s) * I + i (channels fastest, so a 32-wide k block is one
-// filter tap of 32 channels when I % 32 == 0), zero-padded to a multiple of
-// 32 so every k block is a whole 128-byte TMA row.
+// k = (r * S + s) * Ip + i, channels fastest. Ip = I when I % 32 == 0 (a
+// 32-wide k block is one filter tap of 32 channels), else I rounded up to a
+// multiple of 4 with zero weights (every 4-wide, 16-byte k chunk is then 4
+// channels of one tap). The k axis is zero-padded to a multiple of 32 so
+// every k block is a whole 128-byte TMA row.
 Status ConvWeightSplit(const TensorDesc& in, const void* data, TensorDesc* out,
                        std::vector<std::uint8_t>* bytes) {
   if (in.shape.size() != 4 || in.dtype != DataType::kFloat32) {
     return Status::ShapeError("conv_w_tf32x2_okpad expects an OIHW float32 constant");
   }
-  const int64_t O = in.shape[0], I = in.shape[1], R = in.shape[2], S = in.shape[3];
-  const int64_t K = I * R * S;
+  const int64_t O = in.shape[0], I0 = in.shape[1], R = in.shape[2], S = in.shape[3];
+  const int64_t Ip = I0 % 32 == 0 ? I0 : (I0 + 3) / 4 * 4;
+  const int64_t K = Ip * R * S;
   const int64_t Kpad = (K + 31) / 32 * 32;
   const std::size_t plane = static_cast<std::size_t>(O * Kpad);
   *out = TensorDesc({2, O, Kpad}, DataType::kFloat32, in.device_type, in.device_id, "");
@@ -60,12 +63,12 @@ Status ConvWeightSplit(const TensorDesc& in, const void* data, TensorDesc* out,
   const auto* w = static_cast<const float*>(data);
   auto* dst = reinterpret_cast<float*>(bytes->data());
   for (int64_t o = 0; o < O; ++o)
-    for (int64_t i = 0; i < I; ++i)
+    for (int64_t i = 0; i < I0; ++i)
       for (int64_t r = 0; r < R; ++r)
         for (int64_t s = 0; s < S; ++s) {
           float hi, lo;
-          SplitTf32(w[((o * I + i) * R + r) * S + s], &hi, &lo);
-          const std::size_t at = static_cast<std::size_t>(o * Kpad + (r * S + s) * I + i);
+          SplitTf32(w[((o * I0 + i) * R + r) * S + s], &hi, &lo);
+          const std::size_t at = static_cast<std::size_t>(o * Kpad + (r * S + s) * Ip + i);
           dst[at] = hi;
           dst[plane + at] = lo;
         }

@@ -62,6 +62,8 @@ _GRID_FIELDS = {
     "meta": {"kind", "name"},
     "ceil_div": {"kind", "args"},
     "mul": {"kind", "args"},
+    "min": {"kind", "args"},
+    "sm_count": {"kind"},
 }
 _PREPACKS = {"transpose_2d", "conv_w_tf32x2_okpad", "gemm_w_tf32x2_nk"}
 
@@ -173,7 +175,7 @@ def _validate_grid(kernel_id: str, node: dict[str, Any], depth: int) -> None:
     kind = node.get("kind")
     if kind not in _GRID_FIELDS or set(node) - _GRID_FIELDS[kind]:
         raise ValueError(f"{kernel_id}: unsafe grid expression {node}")
-    if kind in {"ceil_div", "mul"}:
+    if kind in {"ceil_div", "mul", "min"}:
         if len(node.get("args", ())) != 2:
             raise ValueError(f"{kernel_id}: {kind} needs two operands")
         for arg in node["args"]:

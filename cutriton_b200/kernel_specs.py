@@ -104,18 +104,18 @@ def _conv_specs() -> list[KernelSpec]:
          (tma_w,) + x + BN_TENSORS + (arg("residual", "*fp32", "input", index=6),) + out + CONV_DIMS
          + (EPSILON,) + RESERVED),
     ]
-    tc_grid = (
-        ceil_div(mul(out_dim(0), mul(out_dim(2), out_dim(3))), meta("BLOCK_PIXELS")),
-        ceil_div(out_dim(1), meta("BLOCK_CHANNELS")),
-    )
+    # Persistent: min(#tiles, #SMs) CTAs walk the 128-channel x 128-pixel tiles.
+    tiles = mul(ceil_div(mul(out_dim(0), mul(out_dim(2), out_dim(3))), meta("BLOCK_PIXELS")),
+                ceil_div(out_dim(1), meta("BLOCK_CHANNELS")))
+    tc_grid = ({"kind": "min", "args": [tiles, {"kind": "sm_count"}]},)
     for kernel_id, op_type, symbol, arguments in tc_families:
         stages = 3
+        smem = stages * 65536 + 4 * 32 * 33 * 4 + 1024 + 256
         specs.append(KernelSpec(
             kernel_id=kernel_id, op_type=op_type, version=1, source="conv_tc.cu", symbol=symbol,
             arguments=arguments, grid=tc_grid, layout="NCHW",
             constraints=({"kind": "input_is_constant", "index": 1},),
-            variants=(Variant(f"m128n128k32s{stages}_3xtf32", num_warps=8,
-                              shared_memory_bytes=stages * 65536 + 1024 + 256,
+            variants=(Variant(f"persistent_m128n128k32s{stages}_3xtf32", num_warps=10, shared_memory_bytes=smem,
                               meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128},
                               defines={"CTB_STAGES": str(stages)}, default=True),),
         ))

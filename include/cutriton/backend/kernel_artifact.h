@@ -99,6 +99,9 @@ enum class GridExpressionKind {
   kVariantMeta,
   kCeilDiv,
   kMultiply,
+  // sm_100a extensions: persistent kernels size their grid to the device.
+  kMinimum,         ///< min of two sub-expressions
+  kDeviceSmCount,   ///< multiprocessor count of the launch device
 };
 
 // Restricted launch-grid expression tree (no code from the manifest runs).
