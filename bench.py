@@ -134,14 +134,26 @@ def barrier(world: int) -> None:
 
 
 def max_over_ranks(value: float, world: int) -> float:
+    """Slowest rank's value (device time of the timed region)."""
     if world == 1:
         return value
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def shard(global_batch: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous batch shard of `rank`: (first image, image count). Every
+    rank gets global_batch // world images; the first global_batch % world
+    ranks take one more."""
+    base, extra = divmod(global_batch, world)
+    count = base + (1 if rank < extra else 0)
+    start = rank * base + min(rank, extra)
+    return start, count
 
 
 def kernel_launches_per_run(engine, ctx) -> int:
