@@ -151,8 +151,11 @@ class Model:
         self._h = handle
 
     def __del__(self) -> None:
-        if getattr(self, "_h", None):
-            library().ctb_model_destroy(self._h)
+        if getattr(self, "_h", None) and _lib is not None:
+            try:
+                _lib.ctb_model_destroy(self._h)
+            except Exception:  # interpreter shutdown
+                pass
             self._h = None
 
     def add_input(self, name: str, shape: Sequence[int], dtype=np.float32, layout: str = "NCHW") -> None:
@@ -210,8 +213,11 @@ class Engine:
         self._h = handle
 
     def __del__(self) -> None:
-        if getattr(self, "_h", None):
-            library().ctb_engine_destroy(self._h)
+        if getattr(self, "_h", None) and _lib is not None:
+            try:
+                _lib.ctb_engine_destroy(self._h)
+            except Exception:  # interpreter shutdown
+                pass
             self._h = None
 
     def num_ops(self) -> int:
@@ -266,8 +272,11 @@ class ExecutionContext:
         self._engine = engine  # keeps plan inspection alive; the C++ context does not need it
 
     def __del__(self) -> None:
-        if getattr(self, "_h", None):
-            library().ctb_context_destroy(self._h)
+        if getattr(self, "_h", None) and _lib is not None:
+            try:
+                _lib.ctb_context_destroy(self._h)
+            except Exception:  # interpreter shutdown
+                pass
             self._h = None
 
     def bind_input(self, name: str, device_ptr: int, nbytes: int) -> None:
