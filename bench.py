@@ -51,7 +51,69 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--no-ffn", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
+                   help="run one small kernel case three times (for ncu captures) and exit")
     return p.parse_args()
+
+
+def _conv_case(n, c, h, k, r, stride, pad, op="FusedConvBatchNormRelu"):
+    """One convolution node through the engine; returns (engine, ctx, tensors)."""
+    import torch
+    import cutriton_b200 as ct
+
+    rng = np.random.default_rng(0)
+    m = ct.Model()
+    m.add_input("x", [n, c, h, h])
+    m.add_constant("w", (rng.standard_normal((k, c, r, r)) * 0.05).astype(np.float32), layout="OIHW")
+    for nm in ("s", "b", "mu", "v"):
+        m.add_constant(nm, np.ones(k, np.float32), layout="")
+    m.add_node("conv", op, ["x", "w", "s", "b", "mu", "v"], ["y"], strides=[stride, stride],
+               pads=[pad] * 4, dilations=[1, 1], batchnorm_epsilon=1e-5)
+    m.add_output("y")
+    e = ct.build_engine(m, enable_cuda_graph=False, tuning_mode=ct.TUNING_DISABLED)
+    ctx = e.create_context()
+    ho = (h + 2 * pad - r) // stride + 1
+    x = torch.randn(n, c, h, h, device="cuda")
+    y = torch.empty(n, k, ho, ho, device="cuda")
+    ctx.bind_tensor("x", x)
+    ctx.bind_tensor("y", y, output=True)
+    return e, ctx, (x, y)
+
+
+def _ffn_case():
+    import torch
+    import cutriton_b200 as ct
+    from cutriton_b200 import workloads
+
+    t, h, i = FFN["tokens"], FFN["hidden"], FFN["inner"]
+    e = ct.build_engine(workloads.build_ffn(workloads.ffn_weights(h, i), t, h, i),
+                        enable_cuda_graph=False, tuning_mode=ct.TUNING_DISABLED)
+    ctx = e.create_context()
+    x = torch.from_numpy(workloads.ffn_input(t, h)).cuda()
+    y = torch.empty(t, h, dtype=torch.float16, device="cuda")
+    ctx.bind_tensor("x", x)
+    ctx.bind_tensor("output", y, output=True)
+    return e, ctx, (x, y)
+
+
+# Small single-kernel cases for ncu captures (a few hundred MB on the device).
+PROFILE_CASES = {
+    "conv3x3_128ch_28x28_bs64": lambda: _conv_case(64, 128, 28, 128, 3, 1, 1),
+    "conv1x1_256to64_56x56_bs32": lambda: _conv_case(32, 256, 56, 64, 1, 1, 0),
+    "stem7x7_bs16": lambda: _conv_case(16, 3, 224, 64, 7, 2, 3),
+    "ffn_4096x768x3072": _ffn_case,
+}
+
+
+def run_profile_case(name: str) -> None:
+    import torch
+
+    keep = PROFILE_CASES[name]()
+    ctx = keep[1]
+    for _ in range(3):
+        ctx.run()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": name, "runs": 3}), flush=True)
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -357,6 +419,9 @@ def base_line(args, world) -> dict:
 
 def main() -> None:
     args = parse_args()
+    if args.profile_case:
+        run_profile_case(args.profile_case)
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -108,6 +108,21 @@ def _conv_specs() -> list[KernelSpec]:
     tiles = mul(ceil_div(mul(out_dim(0), mul(out_dim(2), out_dim(3))), meta("BLOCK_PIXELS")),
                 ceil_div(out_dim(1), meta("BLOCK_CHANNELS")))
     tc_grid = ({"kind": "min", "args": [tiles, {"kind": "sm_count"}]},)
+    # Activation operand in TMEM (pixels on M, channels on N): the default.
+    # BLOCK_CHANNELS=128 counts the tiles for both of the kernel's channel
+    # tilings (64 when Cout <= 64, else 128).
+    tma_w64 = arg("tma_w", "tensormap", "tensor_map", tensor="input", index=1, box=[32, 64, 1], swizzle=128,
+                  prepack="conv_w_tf32x2_okpad")
+    tm_smem = 131072 + 1536 + 256 + 1024
+    for kernel_id, op_type, symbol, arguments in tc_families:
+        specs.append(KernelSpec(
+            kernel_id=kernel_id.replace("tcgen05", "tcgen05_tmem"), op_type=op_type, version=1,
+            source="conv_tm.cu", symbol=symbol.replace("_tc", "_tm"),
+            arguments=(tma_w64,) + arguments[1:], grid=tc_grid, layout="NCHW",
+            constraints=({"kind": "input_is_constant", "index": 1},),
+            variants=(Variant("persistent_m128n128k32_tmem_a_3xtf32", num_warps=14, shared_memory_bytes=tm_smem,
+                              meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, default=True),),
+        ))
     for kernel_id, op_type, symbol, arguments in tc_families:
         stages = 3
         smem = stages * 65536 + 4 * 32 * 33 * 4 + 1024 + 256
@@ -117,7 +132,7 @@ def _conv_specs() -> list[KernelSpec]:
             constraints=({"kind": "input_is_constant", "index": 1},),
             variants=(Variant(f"persistent_m128n128k32s{stages}_3xtf32", num_warps=10, shared_memory_bytes=smem,
                               meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128},
-                              defines={"CTB_STAGES": str(stages)}, default=True),),
+                              defines={"CTB_STAGES": str(stages)}, default=False),),
         ))
     return specs
 

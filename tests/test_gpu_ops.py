@@ -63,6 +63,8 @@ CONV_CASES = [
     (1, 128, 14, 14, 128, 3, 2, 1),   # 3x3 stride 2
     (2, 256, 7, 7, 100, 1, 2, 0),     # 1x1 stride 2, K not multiple of 64
     (1, 37, 9, 11, 19, 3, 1, 1),      # ragged everything
+    (8, 64, 56, 56, 256, 1, 1, 0),    # > 2 persistent tiles per CTA (128-channel tiles)
+    (8, 64, 56, 56, 64, 1, 1, 0),     # > 1 persistent tile per CTA (64-channel tiles)
 ]
 
 
