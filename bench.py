@@ -56,7 +56,7 @@ def parse_args() -> argparse.Namespace:
     return p.parse_args()
 
 
-def _conv_case(n, c, h, k, r, stride, pad, op="FusedConvBatchNormRelu"):
+def _conv_case(n, c, h, k, r, stride, pad, op="FusedConvBatchNormRelu", residual=False):
     """One convolution node through the engine; returns (engine, ctx, tensors)."""
     import torch
     import cutriton_b200 as ct
@@ -67,17 +67,26 @@ def _conv_case(n, c, h, k, r, stride, pad, op="FusedConvBatchNormRelu"):
     m.add_constant("w", (rng.standard_normal((k, c, r, r)) * 0.05).astype(np.float32), layout="OIHW")
     for nm in ("s", "b", "mu", "v"):
         m.add_constant(nm, np.ones(k, np.float32), layout="")
-    m.add_node("conv", op, ["x", "w", "s", "b", "mu", "v"], ["y"], strides=[stride, stride],
+    ho = (h + 2 * pad - r) // stride + 1
+    names = ["x", "w", "s", "b", "mu", "v"]
+    if residual:
+        op = "FusedConvBatchNormAddRelu"
+        m.add_input("res", [n, k, ho, ho])
+        names.append("res")
+    m.add_node("conv", op, names, ["y"], strides=[stride, stride],
                pads=[pad] * 4, dilations=[1, 1], batchnorm_epsilon=1e-5)
     m.add_output("y")
     e = ct.build_engine(m, enable_cuda_graph=False, tuning_mode=ct.TUNING_DISABLED)
     ctx = e.create_context()
-    ho = (h + 2 * pad - r) // stride + 1
     x = torch.randn(n, c, h, h, device="cuda")
     y = torch.empty(n, k, ho, ho, device="cuda")
     ctx.bind_tensor("x", x)
     ctx.bind_tensor("y", y, output=True)
-    return e, ctx, (x, y)
+    keep = [x, y]
+    if residual:
+        keep.append(torch.randn(n, k, ho, ho, device="cuda"))
+        ctx.bind_tensor("res", keep[-1])
+    return e, ctx, keep
 
 
 def _ffn_case():
@@ -96,11 +105,13 @@ def _ffn_case():
     return e, ctx, (x, y)
 
 
-# Small single-kernel cases for ncu captures (a few hundred MB on the device).
+# Single-kernel cases for ncu captures: inputs + outputs above L2 (126 MB), a few
+# hundred MB on the device.
 PROFILE_CASES = {
-    "conv3x3_128ch_28x28_bs64": lambda: _conv_case(64, 128, 28, 128, 3, 1, 1),
-    "conv1x1_256to64_56x56_bs32": lambda: _conv_case(32, 256, 56, 64, 1, 1, 0),
-    "stem7x7_bs16": lambda: _conv_case(16, 3, 224, 64, 7, 2, 3),
+    "conv3x3_128ch_28x28_bs256": lambda: _conv_case(256, 128, 28, 128, 3, 1, 1),
+    "conv1x1_256to64_56x56_bs64": lambda: _conv_case(64, 256, 56, 64, 1, 1, 0),
+    "conv1x1_64to256_add_56x56_bs64": lambda: _conv_case(64, 64, 56, 256, 1, 1, 0, residual=True),
+    "stem7x7_bs64": lambda: _conv_case(64, 3, 224, 64, 7, 2, 3),
     "ffn_4096x768x3072": _ffn_case,
 }
 

@@ -14,6 +14,7 @@
 
 #include <array>
 #include <cstdint>
+#include <cstring>
 #include <fstream>
 #include <limits>
 #include <mutex>
@@ -146,7 +147,10 @@ double AttributeFloat(const Node& node, const KernelArgumentSource& s) {
 
 Status EncodeTensorMap(const Tensor& tensor, const KernelArgumentSource& s, CUtensorMap* map) {
   const TensorDesc& desc = tensor.desc();
-  const std::size_t rank = desc.shape.size();
+  const std::size_t tensor_rank = desc.shape.size();
+  const std::size_t merge = static_cast<std::size_t>(s.merge_inner);
+  if (merge > tensor_rank) return Status::ShapeError("tensor_map merge_inner exceeds the tensor rank");
+  const std::size_t rank = tensor_rank - merge + 1;
   if (rank != s.box.size()) return Status::ShapeError("tensor_map box rank differs from the tensor rank");
   CUtensorMapDataType type;
   switch (desc.dtype) {
@@ -159,20 +163,32 @@ Status EncodeTensorMap(const Tensor& tensor, const KernelArgumentSource& s, CUte
   cuuint64_t strides[4];
   cuuint32_t box[5];
   cuuint32_t element_strides[5];
+  // Innermost (folded) dimension first.
+  int64_t inner = 1;
+  for (std::size_t i = 0; i < merge; ++i) inner *= desc.shape[tensor_rank - 1 - i];
   std::uint64_t running = element;
+  bool aligned = true;
   for (std::size_t i = 0; i < rank; ++i) {
-    const int64_t extent = desc.shape[rank - 1 - i];  // innermost first
+    const int64_t extent = i == 0 ? inner : desc.shape[rank - 1 - i];
     dims[i] = static_cast<cuuint64_t>(extent);
     box[i] = static_cast<cuuint32_t>(s.box[i]);
     element_strides[i] = 1;
-    if (i > 0) strides[i - 1] = running;
+    if (i > 0) {
+      strides[i - 1] = running;
+      aligned = aligned && running % 16 == 0;
+    }
     running *= static_cast<std::uint64_t>(extent);
+  }
+  void* address = reinterpret_cast<void*>(DeviceAddress(tensor));
+  aligned = aligned && reinterpret_cast<std::uintptr_t>(address) % 16 == 0;
+  if (s.optional && !aligned) {
+    std::memset(map, 0, sizeof(*map));
+    return Status::OK();
   }
   CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE;
   if (s.swizzle_bytes == 32) swizzle = CU_TENSOR_MAP_SWIZZLE_32B;
   if (s.swizzle_bytes == 64) swizzle = CU_TENSOR_MAP_SWIZZLE_64B;
   if (s.swizzle_bytes == 128) swizzle = CU_TENSOR_MAP_SWIZZLE_128B;
-  void* address = reinterpret_cast<void*>(DeviceAddress(tensor));
   return drv::Check(drv::Get().cuTensorMapEncodeTiled(
                         map, type, static_cast<cuuint32_t>(rank), address, dims, strides, box,
                         element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,

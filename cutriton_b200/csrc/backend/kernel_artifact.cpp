@@ -196,6 +196,9 @@ KernelArgumentSpec ParseArgument(const json::Value& v) {
     s.map_output = tensor == "output";
     s.box = IntList(src.at("box"));
     s.swizzle_bytes = IntOr(src, "swizzle", 0);
+    s.merge_inner = static_cast<int>(IntOr(src, "merge_inner", 1));
+    s.optional = IntOr(src, "optional", 0) != 0;
+    if (s.merge_inner < 1 || s.merge_inner > 4) throw std::runtime_error("tensor_map merge_inner must be 1..4");
     if (s.box.empty() || s.box.size() > 5) throw std::runtime_error("tensor_map box rank must be 1..5");
     for (int64_t extent : s.box) {
       if (extent <= 0 || extent > 256) throw std::runtime_error("tensor_map box extent must be 1..256");

@@ -75,6 +75,40 @@ Status ConvWeightSplit(const TensorDesc& in, const void* data, TensorDesc* out,
   return Status::OK();
 }
 
+// OIHW fp32 weights -> [2][O][Kpad] (hi, lo) with the k order of the
+// TMEM-operand convolution. When I % 32 == 0 the k blocks walk the filter
+// taps inside each 32-channel block: k = ((i / 32) * R * S + r * S + s) * 32
+// + i % 32, so consecutive k blocks of one pixel tile re-read the same 32
+// input channel planes (shifted by one tap) and hit in L1. Other channel
+// counts keep the tap-major order of conv_w_tf32x2_okpad.
+Status ConvWeightSplitChannelBlocks(const TensorDesc& in, const void* data, TensorDesc* out,
+                                    std::vector<std::uint8_t>* bytes) {
+  if (in.shape.size() != 4 || in.dtype != DataType::kFloat32) {
+    return Status::ShapeError("conv_w_tf32x2_cb expects an OIHW float32 constant");
+  }
+  const int64_t I0 = in.shape[1];
+  if (I0 % 32 != 0) return ConvWeightSplit(in, data, out, bytes);
+  const int64_t O = in.shape[0], R = in.shape[2], S = in.shape[3];
+  const int64_t Kpad = I0 * R * S;  // already a multiple of 32
+  const std::size_t plane = static_cast<std::size_t>(O * Kpad);
+  *out = TensorDesc({2, O, Kpad}, DataType::kFloat32, in.device_type, in.device_id, "");
+  bytes->assign(2 * plane * sizeof(float), 0);
+  const auto* w = static_cast<const float*>(data);
+  auto* dst = reinterpret_cast<float*>(bytes->data());
+  for (int64_t o = 0; o < O; ++o)
+    for (int64_t i = 0; i < I0; ++i)
+      for (int64_t r = 0; r < R; ++r)
+        for (int64_t s = 0; s < S; ++s) {
+          float hi, lo;
+          SplitTf32(w[((o * I0 + i) * R + r) * S + s], &hi, &lo);
+          const int64_t k = ((i / 32) * R * S + r * S + s) * 32 + i % 32;
+          const std::size_t at = static_cast<std::size_t>(o * Kpad + k);
+          dst[at] = hi;
+          dst[plane + at] = lo;
+        }
+  return Status::OK();
+}
+
 // [K, N] fp32 GEMM weights -> [2][N][K] (hi, lo) K-major TF32 split.
 Status GemmWeightSplit(const TensorDesc& in, const void* data, TensorDesc* out,
                        std::vector<std::uint8_t>* bytes) {
@@ -101,6 +135,7 @@ const std::unordered_map<std::string, Transform>& Registry() {
   static const std::unordered_map<std::string, Transform> table = {
       {"transpose_2d", Transpose2d},
       {"conv_w_tf32x2_okpad", ConvWeightSplit},
+      {"conv_w_tf32x2_cb", ConvWeightSplitChannelBlocks},
       {"gemm_w_tf32x2_nk", GemmWeightSplit},
   };
   return table;

@@ -2,9 +2,13 @@
 // GEMM on the 5th-generation tensor cores with the activation operand held in
 // tensor memory (TMEM), NCHW / OIHW.
 //
-// GEMM view: D[pixel, co] = sum_k X_im2col[pixel, k] * W[co, k] with
-// k = (r * S + s) * Cp + c (Cp = C when C % 32 == 0, else C rounded up to a
-// multiple of 4; padded channels carry zero weights). FP32 accuracy from TF32
+// GEMM view: D[pixel, co] = sum_k X_im2col[pixel, k] * W[co, k]. When
+// C % 32 == 0 the k blocks walk the filter taps inside each 32-channel block,
+// k = ((c / 32) * R * S + r * S + s) * 32 + c % 32, so successive blocks of a
+// pixel tile read the same 32 channel planes shifted by one tap (L1 hits);
+// otherwise k = (r * S + s) * Cp + c with Cp = C rounded up to a multiple of 4
+// (padded channels carry zero weights) and a per-CTA table in shared memory
+// maps each 4-wide k chunk to its (r, s, c). FP32 accuracy from TF32
 // units: each operand is split x = hi + lo (hi = x with the low 13 mantissa
 // bits cleared, exact in TF32; lo = x - hi) and D accumulates
 // hi*hi + hi*lo + lo*hi in FP32.
@@ -59,7 +63,13 @@ constexpr uint32_t kBoxBytes = kBoxRows * kBK * 4;  // 8 KB
 constexpr uint32_t kTmemCols = 512;
 constexpr int kMaxStages = 6;
 constexpr uint32_t kStageRegionBytes = 131072;      // max over configurations
-constexpr uint32_t kParamBytes = 4 * 32 * 4 * 3;    // per epilogue warp: mean, scale, bias x 32
+constexpr int kChunkTable = 256;                     // 4-wide k chunks described in shared memory
+// Epilogue staging ring: kSlots slots of [32 channels][128 pixels] FP32; the
+// residual is loaded kLoadAhead chunks ahead, so a slot is refilled two
+// chunks after its store was issued.
+constexpr int kSlots = 6;
+constexpr int kLoadAhead = 4;
+constexpr uint32_t kStagingBytes = kSlots * 32 * 128 * 4;
 
 template <int BN>
 struct Tile {
@@ -83,11 +93,13 @@ struct __align__(8) Barriers {
   uint64_t empty[kMaxStages];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
+  uint64_t residual_full[6];  // bulk residual loads, one per staging slot
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
   int consumed;
 };
+static_assert(sizeof(Barriers) <= 256, "barrier block");
 
 // 32 lanes x 32 consecutive 32-bit columns from registers: thread t of the
 // warp writes row (lane base + t).
@@ -116,6 +128,23 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
+// Named barrier 1 over the four epilogue warps (128 threads).
+__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// OR of `pred` over the four epilogue warps; all of them get the same answer.
+__device__ __forceinline__ bool epilogue_any(bool pred) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, 128, p;\n\t"
+      "selp.b32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<int>(pred))
+      : "memory");
+  return r != 0;
+}
+
 struct PixelSource {
   const float* image;
   int ih0, iw0;
@@ -136,49 +165,86 @@ __device__ __forceinline__ PixelSource pixel_source(const float* x, const ConvSh
   return px;
 }
 
+// Predicated read-only load, kept in program order (asm volatile) so each
+// block's loads are issued a whole block ahead of their use.
+__device__ __forceinline__ float load_or_zero(const float* ptr, bool pred) {
+  float v;
+  asm volatile(
+      "{\n\t.reg .pred q;\n\t"
+      "setp.ne.b32 q, %2, 0;\n\t"
+      "mov.b32 %0, 0;\n\t"
+      "@q ld.global.nc.f32 %0, [%1];\n\t}"
+      : "=f"(v)
+      : "l"(ptr), "r"(static_cast<int>(pred)));
+  return v;
+}
+
+// (r, s, c) of a 4-wide k chunk, packed c << 20 | r << 10 | s; -1 past kdim.
+__device__ __forceinline__ int chunk_entry(int k, int cp, int kdim, int s_dim) {
+  if (k >= kdim) return -1;
+  const int tap = k / cp;
+  const int r = tap / s_dim;
+  return ((k - tap * cp) << 20) | (r << 10) | (tap - r * s_dim);
+}
+
 // Loads the 32 k values of block `kb` for one pixel (im2col, zero padding).
 __device__ __forceinline__ void gather_block(const PixelSource& px, const ConvShape& p, int cp, int kdim,
-                                             long long plane, int kb, float (&v)[kBK]) {
+                                             long long plane, int kb, const int* table, float (&v)[kBK]) {
   if (p.c % kBK == 0) {
-    // One filter tap, 32 consecutive channels.
-    const int k0 = kb * kBK;
-    const int tap = k0 / cp;
-    const int c0 = k0 - tap * cp;
+    // One filter tap, 32 consecutive channels of one channel block.
+    const int taps = p.r * p.s;
+    const int cb = kb / taps;
+    const int tap = kb - cb * taps;
     const int r = tap / p.s;
     const int ih = px.ih0 + r * p.dil_h;
     const int iw = px.iw0 + (tap - r * p.s) * p.dil_w;
     const bool inside = px.valid && ih >= 0 && ih < p.h && iw >= 0 && iw < p.w;
-    const float* src = px.image + static_cast<long long>(c0) * plane + static_cast<long long>(ih) * p.w + iw;
+    const float* src =
+        px.image + static_cast<long long>(cb * kBK) * plane + static_cast<long long>(ih) * p.w + iw;
 #pragma unroll
-    for (int kk = 0; kk < kBK; ++kk) v[kk] = inside ? __ldg(src + kk * plane) : 0.0f;
+    for (int kk = 0; kk < kBK; ++kk) v[kk] = load_or_zero(src + kk * plane, inside);
   } else {
     // Chunks of 4 k: four channels of one tap (cp is a multiple of 4).
 #pragma unroll
     for (int j = 0; j < kBK / 4; ++j) {
-      const int k = kb * kBK + 4 * j;
-      const int tap = k / cp;
-      const int c = k - tap * cp;
-      const int r = tap / p.s;
+      int c, r, s_tap;
+      bool in_k;
+      if (table != nullptr) {
+        const int e = table[kb * (kBK / 4) + j];
+        in_k = e >= 0;
+        c = e >> 20;
+        r = (e >> 10) & 1023;
+        s_tap = e & 1023;
+      } else {
+        const int k = kb * kBK + 4 * j;
+        const int tap = k / cp;
+        in_k = k < kdim;
+        c = k - tap * cp;
+        r = tap / p.s;
+        s_tap = tap - r * p.s;
+      }
       const int ih = px.ih0 + r * p.dil_h;
-      const int iw = px.iw0 + (tap - r * p.s) * p.dil_w;
-      const bool inside = px.valid && k < kdim && ih >= 0 && ih < p.h && iw >= 0 && iw < p.w;
+      const int iw = px.iw0 + s_tap * p.dil_w;
+      const bool inside = px.valid && in_k && ih >= 0 && ih < p.h && iw >= 0 && iw < p.w;
       const float* src = px.image + static_cast<long long>(c) * plane + static_cast<long long>(ih) * p.w + iw;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[4 * j + i] = (inside && c + i < p.c) ? __ldg(src + i * plane) : 0.0f;
+      for (int i = 0; i < 4; ++i) v[4 * j + i] = load_or_zero(src + i * plane, inside && c + i < p.c);
     }
   }
 }
 
 template <int kEpilogue, int BN>
-__device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_w, const float* __restrict__ x,
+__device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_w, const TmaDescriptor* tma_out,
+                                        const TmaDescriptor* tma_res, const float* __restrict__ x,
                                         const float* __restrict__ scale, const float* __restrict__ bias,
                                         const float* __restrict__ mean, const float* __restrict__ variance,
                                         const float* __restrict__ residual, float* __restrict__ out,
                                         const ConvShape& p, float epsilon, void* scratch) {
   using T = Tile<BN>;
   constexpr int kStages = T::kStages;
-  float* params = reinterpret_cast<float*>(smem + kStageRegionBytes);
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStageRegionBytes + kParamBytes);
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStageRegionBytes);
+  int* chunk_table = reinterpret_cast<int*>(smem + kStageRegionBytes + 256);
+  float* staging = reinterpret_cast<float*>(smem + kStageRegionBytes + 256 + kChunkTable * 4);
   volatile int* abort = &bars->abort;
   auto b_hi = [&](int s) { return smem + s * T::kStageBytes; };
   auto b_lo = [&](int s) { return smem + s * T::kStageBytes + T::kPlaneBytes; };
@@ -193,6 +259,11 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
   const int co_tiles = (p.k + BN - 1) / BN;
   const long long tiles = ((total_pixels + kBM - 1) / kBM) * co_tiles;
   const int my_tiles = tiles > blockIdx.x ? static_cast<int>((tiles - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+  // Bulk / tensor-copy epilogue: needs 16-byte aligned rows of every channel
+  // plane, the same condition under which the host encodes tma_out / tma_res
+  // (otherwise they are bound as zeros and must not be touched).
+  const bool bulk_epilogue = pixels_per_image % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                             (kEpilogue != kBatchNormAddRelu || (reinterpret_cast<uintptr_t>(residual) & 15) == 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -204,11 +275,22 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       mbar_init(&bars->tmem_full[b], 1);
       mbar_init(&bars->tmem_empty[b], 4);
     }
+    for (int b = 0; b < kSlots; ++b) mbar_init(&bars->residual_full[b], 32);  // 8 issuing lanes x 4 warps
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
     bars->consumed = 0;
     mbar_init_fence();
     tma_prefetch(tma_w);
+    if (bulk_epilogue) {
+      tma_prefetch(tma_out);
+      if (kEpilogue == kBatchNormAddRelu) tma_prefetch(tma_res);
+    }
+  }
+  // Small / ragged channel counts: describe every 4-wide k chunk once.
+  const bool use_table = p.c % kBK != 0 && k_blocks * (kBK / 4) <= kChunkTable && cp < 4096 && p.r < 1024 &&
+                         p.s < 1024;
+  if (use_table) {
+    for (int i = threadIdx.x; i < k_blocks * (kBK / 4); i += blockDim.x) chunk_table[i] = chunk_entry(4 * i, cp, kdim, p.s);
   }
   if (warp == 0) tmem_alloc(&bars->tmem_base, kTmemCols);
   tc_fence_before_sync();
@@ -229,31 +311,43 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       const long long tile = blockIdx.x + static_cast<long long>(local) * gridDim.x;
       const PixelSource px =
           pixel_source(x, p, (tile / co_tiles) * kBM + row, total_pixels, pixels_per_image);
-      gather_block(px, p, cp, kdim, plane, kb, v);
+      gather_block(px, p, cp, kdim, plane, kb, use_table ? chunk_table : nullptr, v);
     };
-    float cur[kBK], nxt[kBK];
-    int item = group;
-    if (item < items) fetch(item, cur);
-    for (; item < items; item += 2) {
-      if (item + 2 < items) fetch(item + 2, nxt);
+    // Splits one block into hi / lo and writes it to the stage's TMEM columns.
+    // Returns false when the kernel is aborting.
+    auto publish = [&](int item, float (&v)[kBK]) -> bool {
       const int s = item % kStages;
       const int use = item / kStages;
-      if (use > 0 && !mbar_wait(&bars->empty[s], (use - 1) & 1, abort, scratch, 30)) break;
+      if (use > 0 && !mbar_wait(&bars->empty[s], (use - 1) & 1, abort, scratch, 30)) return false;
       tc_fence_after_sync();
       const uint32_t a_col = tmem + lane_bits + T::kAColumn0 + s * 2 * kBK;
-      uint32_t hi[kBK], lo[kBK];
+      uint32_t hi[kBK];
 #pragma unroll
-      for (int kk = 0; kk < kBK; ++kk) {
-        hi[kk] = __float_as_uint(cur[kk]) & 0xFFFFE000u;
-        lo[kk] = __float_as_uint(cur[kk] - __uint_as_float(hi[kk]));
-      }
+      for (int kk = 0; kk < kBK; ++kk) hi[kk] = __float_as_uint(v[kk]) & 0xFFFFE000u;
       tmem_store_32x32(a_col, hi);
-      tmem_store_32x32(a_col + kBK, lo);
+      // lo = v - hi, in place (v is refilled by the next fetch).
+#pragma unroll
+      for (int kk = 0; kk < kBK; ++kk) v[kk] -= __uint_as_float(hi[kk]);
+      tmem_store_32x32(a_col + kBK, reinterpret_cast<uint32_t(&)[kBK]>(v));
       tmem_store_wait();
       tc_fence_before_sync();
       mbar_arrive(&bars->full_a[s]);
-#pragma unroll
-      for (int kk = 0; kk < kBK; ++kk) cur[kk] = nxt[kk];
+      return true;
+    };
+    // Ping-pong register buffers: the group's next block is in flight while
+    // the current one is split and stored (no register copy between them, so
+    // nothing waits on the prefetch early).
+    float buf_a[kBK], buf_b[kBK];
+    int item = group;
+    if (item < items) fetch(item, buf_a);
+    while (item < items) {
+      if (item + 2 < items) fetch(item + 2, buf_b);
+      if (!publish(item, buf_a)) break;
+      item += 2;
+      if (item >= items) break;
+      if (item + 2 < items) fetch(item + 2, buf_a);
+      if (!publish(item, buf_b)) break;
+      item += 2;
     }
   } else if (warp == 0 && lane == 0) {
     // ---- TMA producer: weight hi / lo tiles ----
@@ -330,68 +424,269 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     }
   } else if (warp >= kEpilogueWarp0 && warp < kEpilogueWarp0 + 4) {
     // ---- epilogue: lane = output pixel, 32 channels per TMEM load ----
-    const int quarter = warp & 3;  // TMEM lanes this warp may access
-    float* prm = params + (warp - kEpilogueWarp0) * 32 * 3;
-    for (int local = 0; local < my_tiles; ++local) {
-      const int buf = local & 1;
-      const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
-      __syncwarp();
-      if (!ready) break;
-      tc_fence_after_sync();
-      const long long tile = blockIdx.x + static_cast<long long>(local) * gridDim.x;
-      const int co0 = static_cast<int>(tile % co_tiles) * BN;
-      const long long pixel = (tile / co_tiles) * kBM + quarter * 32 + lane;
-      const bool valid = pixel < total_pixels;
-      long long base = 0;  // output offset of (image, channel 0, pixel)
-      if (valid) {
-        const long long img = pixel / pixels_per_image;
-        base = img * p.k * pixels_per_image + (pixel - img * pixels_per_image);
-      }
-      const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        const int ch0 = co0 + c;
-        if (ch0 >= p.k) break;  // warp-uniform
-        if (kEpilogue != kPlain) {
-          const int co = ch0 + lane;
-          float m = 0.0f, a = 0.0f, b = 0.0f;
-          if (co < p.k) {
-            m = mean[co];
-            a = rsqrtf(variance[co] + epsilon) * scale[co];
-            b = bias[co];
-          }
-          prm[lane * 3 + 0] = m;
-          prm[lane * 3 + 1] = a;
-          prm[lane * 3 + 2] = b;
+    const int quarter = warp & 3;          // TMEM lanes this warp may access
+    const int ew = warp - kEpilogueWarp0;  // 0..3: which channel rows this warp copies
+    constexpr int kChunks = BN / 32;
+    // Folded BatchNorm terms of channel co0 + 32 i + lane, kept in registers
+    // and broadcast with shuffles; reloaded only when the channel tile changes.
+    float pm[kChunks], pa[kChunks], pb[kChunks];
+    int prm_co0 = -1;
+    auto load_params = [&](int co0) {
+      if (kEpilogue == kPlain || co0 == prm_co0) return;
+#pragma unroll
+      for (int i = 0; i < kChunks; ++i) {
+        const int co = co0 + 32 * i + lane;
+        pm[i] = 0.0f;
+        pa[i] = 0.0f;
+        pb[i] = 0.0f;
+        if (co < p.k) {
+          pm[i] = mean[co];
+          pa[i] = rsqrtf(variance[co] + epsilon) * scale[co];
+          pb[i] = bias[co];
         }
-        uint32_t accv[32];
-        tmem_load_32x32(taddr + c, accv);
+      }
+      prm_co0 = co0;
+    };
+    // BN affine, residual (from the staging slot) and ReLU of one chunk, in
+    // place in v (lane = pixel). The slot reads all precede any store.
+    auto finish_chunk = [&](int ci, const float* slot_px, uint32_t (&v)[32]) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float x = __uint_as_float(v[j]);
+        if (kEpilogue != kPlain) {
+          x = (x - __shfl_sync(0xffffffffu, pm[ci], j)) * __shfl_sync(0xffffffffu, pa[ci], j) +
+              __shfl_sync(0xffffffffu, pb[ci], j);
+        }
+        if (kEpilogue == kBatchNormAddRelu) x += slot_px[j * kBM];
+        if (kEpilogue == kBatchNormRelu || kEpilogue == kBatchNormAddRelu) x = fmaxf(x, 0.0f);
+        v[j] = __float_as_uint(x);
+      }
+    };
+    auto tile_index = [&](int local) { return blockIdx.x + static_cast<long long>(local) * gridDim.x; };
+
+    if (bulk_epilogue) {
+      // Bulk path: every 4-pixel group lies inside one image, so each channel
+      // row of a tile is one or a few 16-byte-aligned runs in global memory.
+      // Chunks (32 channels of a tile) go through a ring of kSlots staging
+      // slots in shared memory ([32 channels][128 pixels] each). Chunk h: its
+      // residual was bulk-loaded into slot h % kSlots four chunks earlier; the
+      // result is written in place and leaves with one cp.async.bulk store per
+      // run; then, once the store of chunk h - 2 has been read out, the
+      // residual of chunk h + 4 is loaded into that slot. Lanes 0-7 of each
+      // warp own channel row ew * 8 + lane of every chunk.
+      const bool issuer = lane < 8;
+      const int row = ew * 8 + lane;
+      const int total_chunks = my_tiles * kChunks;
+      // Calls fn(smem_offset_px, global_offset, pixels) for each run of
+      // channel `ch` of tile `tile` (valid pixels only).
+      auto for_each_run = [&](long long tile, int ch, auto&& fn) {
+        const long long p0 = (tile / co_tiles) * kBM;
+        const int n_valid = static_cast<int>(min(static_cast<long long>(kBM), total_pixels - p0));
+        long long img = p0 / pixels_per_image;
+        int hw = static_cast<int>(p0 - img * pixels_per_image);
+        for (int pos = 0; pos < n_valid; ++img, hw = 0) {
+          const int len = min(n_valid - pos, static_cast<int>(pixels_per_image) - hw);
+          fn(pos, (img * p.k + ch) * pixels_per_image + hw, len);
+          pos += len;
+        }
+      };
+      // A tile whose pixels lie in one image moves each chunk with a single
+      // tensor copy: box {128 pixels, 32 channels, 1 image} of the [N][K][H*W]
+      // view at (hw0, channel, image); pixels past H*W and channels past K are
+      // clipped (stores) or zero-filled (loads). Tiles that straddle images
+      // use one 1D copy per channel run.
+      struct TileSpan {
+        int hw0, img;
+        bool one_image;
+      };
+      auto span_of = [&](long long tile) {
+        const long long p0 = (tile / co_tiles) * kBM;
+        const long long img = p0 / pixels_per_image;
+        const int hw0 = static_cast<int>(p0 - img * pixels_per_image);
+        const int n_valid = static_cast<int>(min(static_cast<long long>(kBM), total_pixels - p0));
+        return TileSpan{hw0, static_cast<int>(img), hw0 + n_valid <= pixels_per_image};
+      };
+      const bool leader = ew == 0 && lane == 0;  // issues the tensor copies
+      auto load_residual = [&](int h) {
+        if (kEpilogue != kBatchNormAddRelu || h >= total_chunks || !issuer) return;
+        const int slot_id = h % kSlots;
+        const long long tile = tile_index(h / kChunks);
+        const int ch = static_cast<int>(tile % co_tiles) * BN + 32 * (h % kChunks) + row;
+        float* slot_row = staging + (slot_id * 32 + row) * kBM;
+        const TileSpan span = span_of(tile);
+        if (span.one_image) {
+          mbar_arrive_expect_tx(&bars->residual_full[slot_id], leader ? 32u * kBM * 4u : 0u);
+          if (leader) {
+            tma_load_3d(staging + slot_id * 32 * kBM, tma_res, &bars->residual_full[slot_id], span.hw0, ch - row,
+                        span.img);
+          }
+          return;
+        }
+        uint32_t bytes = 0;
+        if (ch < p.k) for_each_run(tile, ch, [&](int, long long, int len) { bytes += 4u * len; });
+        mbar_arrive_expect_tx(&bars->residual_full[slot_id], bytes);
+        if (ch < p.k) {
+          for_each_run(tile, ch, [&](int pos, long long goff, int len) {
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_addr(slot_row + pos)),
+                "l"(residual + goff), "r"(4 * len), "r"(smem_addr(&bars->residual_full[slot_id]))
+                : "memory");
+          });
+        }
+      };
+#pragma unroll
+      for (int h = 0; h < kLoadAhead; ++h) load_residual(h);
+      int local = 0;
+      for (; local < my_tiles; ++local) {
+        const int buf = local & 1;
+        const long long tile = tile_index(local);
+        const int co0 = static_cast<int>(tile % co_tiles) * BN;
+        const TileSpan tile_span = span_of(tile);
+        load_params(co0);
+        const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
+        // The four epilogue warps leave together (they share named barriers).
+        if (epilogue_any(!ready)) break;
+        tc_fence_after_sync();
+        const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll
+        for (int ci = 0; ci < kChunks; ++ci) {
+          const int h = local * kChunks + ci;
+          const int slot_id = h % kSlots;
+          float* slot = staging + slot_id * 32 * kBM;
+          if (kEpilogue == kBatchNormAddRelu) {
+            // A timeout here is recorded (abort); the warps still walk the
+            // same barrier sequence and leave at the next tile.
+            mbar_wait(&bars->residual_full[slot_id], (h / kSlots) & 1, abort, scratch, 38);
+          }
+          uint32_t v[32];
+          tmem_load_32x32(taddr + 32 * ci, v);
+          float* slot_px = slot + quarter * 32 + lane;
+          finish_chunk(ci, slot_px, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) slot_px[j * kBM] = __uint_as_float(v[j]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          epilogue_bar();  // the chunk is complete in shared memory
+          if (issuer) {
+            const int ch = co0 + 32 * ci + row;
+            if (tile_span.one_image) {
+              if (leader) {
+                asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                                 reinterpret_cast<uint64_t>(tma_out)),
+                             "r"(smem_addr(slot)), "r"(tile_span.hw0), "r"(co0 + 32 * ci), "r"(tile_span.img)
+                             : "memory");
+              }
+            } else if (ch < p.k) {
+              for_each_run(tile, ch, [&](int pos, long long goff, int len) {
+                asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(out + goff),
+                             "r"(smem_addr(slot + row * kBM + pos)), "r"(4 * len)
+                             : "memory");
+              });
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            // Stores of chunks <= h - 2 have been read out of their slots.
+            asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kSlots - kLoadAhead) : "memory");
+          }
+          epilogue_bar();
+          load_residual(h + kLoadAhead);  // into slot (h - 2) % kSlots
+        }
+        // Hand the accumulator back to the issuer.
+        tc_fence_before_sync();
         __syncwarp();
-        const int rows = min(32, p.k - ch0);
-        float res[32];
-        if (kEpilogue == kBatchNormAddRelu) {
+        if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
+      }
+      if (issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+      if (kEpilogue == kBatchNormAddRelu && issuer) {
+        // Residual loads issued for chunks that were not reached (abort) must
+        // land before the CTA's shared memory is released.
+        const int consumed = local * kChunks;
+        const int issued = min(total_chunks, consumed + kLoadAhead);
+        for (int h = consumed; h < issued; ++h) {
+          volatile int never = 0;
+          mbar_wait(&bars->residual_full[h % kSlots], (h / kSlots) & 1, &never, scratch, 39);
+        }
+      }
+    } else {
+      // Register path (pixels per image not a multiple of 4): residual
+      // copied with 4-byte cp.async into the staging slots one tile ahead
+      // (slot ci = chunk ci as [32 channels][128 pixels], channel rows split
+      // over the four warps), results stored straight from registers.
+      auto prefetch_residual = [&](int local, int ci) {
+        if (kEpilogue != kBatchNormAddRelu) return;
+        if (local < my_tiles) {
+          const long long tile = tile_index(local);
+          const int ch_base = static_cast<int>(tile % co_tiles) * BN + 32 * ci;
+          const long long p0 = (tile / co_tiles) * kBM;
+          float* slot = staging + ci * 32 * kBM;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const long long px = p0 + 32 * q + lane;
+            const bool pix_ok = px < total_pixels;
+            long long src0 = 0;
+            if (pix_ok) {
+              const long long img = px / pixels_per_image;
+              src0 = img * p.k * pixels_per_image + (px - img * pixels_per_image);
+            }
+#pragma unroll
+            for (int j = ew; j < 32; j += 4) {
+              const bool in = pix_ok && ch_base + j < p.k;
+              const float* src = in ? residual + src0 + static_cast<long long>(ch_base + j) * pixels_per_image
+                                    : residual;
+              asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(
+                               smem_addr(slot + j * kBM + 32 * q + lane)),
+                           "l"(src), "r"(in ? 4 : 0)
+                           : "memory");
+            }
+          }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+      };
+#pragma unroll
+      for (int ci = 0; ci < kChunks; ++ci) prefetch_residual(0, ci);
+      for (int local = 0; local < my_tiles; ++local) {
+        const int buf = local & 1;
+        const long long tile = tile_index(local);
+        const int co0 = static_cast<int>(tile % co_tiles) * BN;
+        const long long pixel = (tile / co_tiles) * kBM + quarter * 32 + lane;
+        const bool valid = pixel < total_pixels;
+        long long base = 0;  // output offset of (image, channel 0, pixel)
+        if (valid) {
+          const long long img = pixel / pixels_per_image;
+          base = img * p.k * pixels_per_image + (pixel - img * pixels_per_image);
+        }
+        load_params(co0);
+        const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
+        if (epilogue_any(!ready)) break;
+        tc_fence_after_sync();
+        const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll
+        for (int ci = 0; ci < kChunks; ++ci) {
+          const int ch0 = co0 + 32 * ci;
+          if (kEpilogue == kBatchNormAddRelu) {
+            asm volatile("cp.async.wait_group %0;" ::"n"(kChunks - 1) : "memory");
+            epilogue_bar();  // every warp's part of chunk ci has landed
+          }
+          uint32_t v[32];
+          tmem_load_32x32(taddr + 32 * ci, v);
+          finish_chunk(ci, staging + ci * 32 * kBM + quarter * 32 + lane, v);
+          if (kEpilogue == kBatchNormAddRelu) {
+            epilogue_bar();  // slot ci is free: refill it for the next tile
+            prefetch_residual(local + 1, ci);
+          }
+          const int rows = min(32, p.k - ch0);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            res[j] = (valid && j < rows) ? __ldg(residual + base + static_cast<long long>(ch0 + j) * pixels_per_image)
-                                         : 0.0f;
+            if (valid && j < rows) {
+              out[base + static_cast<long long>(ch0 + j) * pixels_per_image] = __uint_as_float(v[j]);
+            }
           }
         }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (valid && j < rows) {
-            float v = __uint_as_float(accv[j]);
-            if (kEpilogue != kPlain) v = (v - prm[j * 3 + 0]) * prm[j * 3 + 1] + prm[j * 3 + 2];
-            if (kEpilogue == kBatchNormAddRelu) v += res[j];
-            if (kEpilogue == kBatchNormRelu || kEpilogue == kBatchNormAddRelu) v = fmaxf(v, 0.0f);
-            out[base + static_cast<long long>(ch0 + j) * pixels_per_image] = v;
-          }
-        }
+        tc_fence_before_sync();
         __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
       }
-      // Hand the accumulator back to the issuer.
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
+      // No copy may still be landing in shared memory when the CTA exits.
+      if (kEpilogue == kBatchNormAddRelu) asm volatile("cp.async.wait_all;" ::: "memory");
     }
   }
   tc_fence_before_sync();
@@ -404,16 +699,17 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
 }
 
 template <int kEpilogue>
-__device__ __forceinline__ void conv_tm_dispatch(const TmaDescriptor* tma_w, const float* x, const float* scale,
+__device__ __forceinline__ void conv_tm_dispatch(const TmaDescriptor* tma_w, const TmaDescriptor* tma_out,
+                                                 const TmaDescriptor* tma_res, const float* x, const float* scale,
                                                  const float* bias, const float* mean, const float* variance,
                                                  const float* residual, float* out, const ConvShape& p,
                                                  float epsilon, void* scratch) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   if (p.k <= 64) {
-    conv_tm<kEpilogue, 64>(smem, tma_w, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
+    conv_tm<kEpilogue, 64>(smem, tma_w, tma_out, tma_res, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
   } else {
-    conv_tm<kEpilogue, 128>(smem, tma_w, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
+    conv_tm<kEpilogue, 128>(smem, tma_w, tma_out, tma_res, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
   }
 }
 
@@ -426,36 +722,38 @@ __device__ __forceinline__ void conv_tm_dispatch(const TmaDescriptor* tma_w, con
   ConvShape{n, c, h, w, k, r, s, out_h, out_w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w}
 
 extern "C" __global__ void __launch_bounds__(kThreads, 1)
-ctb_conv_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const float* x, float* output, CTB_CONV_DIMS,
-                CTB_RESERVED_PARAMS) {
+ctb_conv_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const __grid_constant__ TmaDescriptor tma_out,
+                const float* x, float* output, CTB_CONV_DIMS, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kPlain>(&tma_w, x, nullptr, nullptr, nullptr, nullptr, nullptr, output, CTB_CONV_SHAPE, 0.0f,
+  conv_tm_dispatch<kPlain>(&tma_w, &tma_out, nullptr, x, nullptr, nullptr, nullptr, nullptr, nullptr, output, CTB_CONV_SHAPE, 0.0f,
                            runtime_scratch);
 }
 
 extern "C" __global__ void __launch_bounds__(kThreads, 1)
-ctb_conv_bn_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const float* x, const float* scale,
-                   const float* bias, const float* mean, const float* variance, float* output, CTB_CONV_DIMS,
-                   float epsilon, CTB_RESERVED_PARAMS) {
+ctb_conv_bn_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const __grid_constant__ TmaDescriptor tma_out,
+                   const float* x, const float* scale, const float* bias, const float* mean, const float* variance,
+                   float* output, CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kBatchNorm>(&tma_w, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE, epsilon,
+  conv_tm_dispatch<kBatchNorm>(&tma_w, &tma_out, nullptr, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE, epsilon,
                                runtime_scratch);
 }
 
 extern "C" __global__ void __launch_bounds__(kThreads, 1)
-ctb_conv_bn_relu_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const float* x, const float* scale,
-                        const float* bias, const float* mean, const float* variance, float* output,
-                        CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
+ctb_conv_bn_relu_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const __grid_constant__ TmaDescriptor tma_out,
+                        const float* x, const float* scale, const float* bias, const float* mean,
+                        const float* variance, float* output, CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kBatchNormRelu>(&tma_w, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE,
+  conv_tm_dispatch<kBatchNormRelu>(&tma_w, &tma_out, nullptr, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE,
                                    epsilon, runtime_scratch);
 }
 
 extern "C" __global__ void __launch_bounds__(kThreads, 1)
-ctb_conv_bn_add_relu_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const float* x, const float* scale,
+ctb_conv_bn_add_relu_f32_tm(const __grid_constant__ TmaDescriptor tma_w,
+                            const __grid_constant__ TmaDescriptor tma_out,
+                            const __grid_constant__ TmaDescriptor tma_res, const float* x, const float* scale,
                             const float* bias, const float* mean, const float* variance, const float* residual,
                             float* output, CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kBatchNormAddRelu>(&tma_w, x, scale, bias, mean, variance, residual, output, CTB_CONV_SHAPE,
+  conv_tm_dispatch<kBatchNormAddRelu>(&tma_w, &tma_out, &tma_res, x, scale, bias, mean, variance, residual, output, CTB_CONV_SHAPE,
                                       epsilon, runtime_scratch);
 }

@@ -42,7 +42,7 @@ _SOURCE_FIELDS = {
     "attribute_f64": {"kind", "name", "alternate_name", "index", "default"},
     "literal_i32": {"kind", "default"},
     "runtime_reserved": {"kind"},
-    "tensor_map": {"kind", "tensor", "index", "box", "swizzle", "prepack"},
+    "tensor_map": {"kind", "tensor", "index", "box", "swizzle", "prepack", "merge_inner", "optional"},
 }
 _CONSTRAINT_FIELDS = {
     "attribute_i64_eq": {"kind", "name", "value", "default"},
@@ -65,7 +65,7 @@ _GRID_FIELDS = {
     "min": {"kind", "args"},
     "sm_count": {"kind"},
 }
-_PREPACKS = {"transpose_2d", "conv_w_tf32x2_okpad", "gemm_w_tf32x2_nk"}
+_PREPACKS = {"transpose_2d", "conv_w_tf32x2_okpad", "conv_w_tf32x2_cb", "gemm_w_tf32x2_nk"}
 
 
 @dataclass(frozen=True)

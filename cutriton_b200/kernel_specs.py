@@ -112,15 +112,25 @@ def _conv_specs() -> list[KernelSpec]:
     # BLOCK_CHANNELS=128 counts the tiles for both of the kernel's channel
     # tilings (64 when Cout <= 64, else 128).
     tma_w64 = arg("tma_w", "tensormap", "tensor_map", tensor="input", index=1, box=[32, 64, 1], swizzle=128,
-                  prepack="conv_w_tf32x2_okpad")
-    tm_smem = 131072 + 1536 + 256 + 1024
+                  prepack="conv_w_tf32x2_cb")
+    # weight stages + barriers + k-chunk table + epilogue staging ring + alignment slack
+    tm_smem = 131072 + 256 + 1024 + 6 * 16384 + 1024
+    # Epilogue tensor copies over the [N][K][H*W] view (optional: bound as
+    # zeros when H*W*4 is not a multiple of 16; the kernel then stores from
+    # registers).
+    tma_out = arg("tma_out", "tensormap", "tensor_map", tensor="output", index=0, box=[128, 32, 1], merge_inner=2,
+                  optional=1)
+    tma_res = arg("tma_res", "tensormap", "tensor_map", tensor="input", index=6, box=[128, 32, 1], merge_inner=2,
+                  optional=1)
     for kernel_id, op_type, symbol, arguments in tc_families:
+        maps = (tma_w64, tma_out) + ((tma_res,) if op_type.endswith("AddRelu") else ())
         specs.append(KernelSpec(
             kernel_id=kernel_id.replace("tcgen05", "tcgen05_tmem"), op_type=op_type, version=1,
             source="conv_tm.cu", symbol=symbol.replace("_tc", "_tm"),
-            arguments=(tma_w64,) + arguments[1:], grid=tc_grid, layout="NCHW",
+            arguments=maps + arguments[1:], grid=tc_grid, layout="NCHW",
             constraints=({"kind": "input_is_constant", "index": 1},),
-            variants=(Variant("persistent_m128n128k32_tmem_a_3xtf32", num_warps=14, shared_memory_bytes=tm_smem,
+            variants=(Variant("persistent_m128n128k32_tmem_a_3xtf32", num_warps=14,
+                              shared_memory_bytes=tm_smem,
                               meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, default=True),),
         ))
     for kernel_id, op_type, symbol, arguments in tc_families:
