@@ -177,19 +177,26 @@ Status CheckCudaNode(const Node& node, const Graph& graph, const BackendOptions&
 }
 
 // Kernel for one step of an unfused decomposition: the default variant if its
-// constraints hold for the synthesized sub-node, else the first that does.
+// constraints hold for the synthesized sub-node, else another variant of the
+// default kernel, else the first that matches.
 const KernelArtifact* PickSubKernel(const ArtifactRepository& repository, const Node& sub,
                                     const std::string& dtype, const ValueLookup& lookup,
                                     int capability) {
   const auto* list = repository.Find(sub.op_type());
   if (list == nullptr) return nullptr;
+  std::string default_kernel;
+  for (const auto& a : *list) {
+    if (a.dtype == dtype && a.is_default) default_kernel = a.kernel_id;
+  }
+  const KernelArtifact* sibling = nullptr;
   const KernelArtifact* fallback = nullptr;
   for (const auto& a : *list) {
     if (a.dtype != dtype || !ArtifactMatches(a, sub, lookup, capability)) continue;
     if (a.is_default) return &a;
+    if (sibling == nullptr && a.kernel_id == default_kernel) sibling = &a;
     if (fallback == nullptr) fallback = &a;
   }
-  return fallback;
+  return sibling != nullptr ? sibling : fallback;
 }
 
 class CudaSm100Backend final : public Backend {
@@ -230,19 +237,35 @@ class CudaSm100Backend final : public Backend {
     const std::string layout = node.inputs().empty() ? std::string{}
                                                      : graph.FindValue(node.inputs().front())->tensor.layout;
     const ValueLookup lookup = [&](const std::string& n) { return graph.FindValue(n); };
-    for (const KernelArtifact* artifact : context.catalog->Query(node.op_type(), dtype, layout, capability)) {
+    const auto artifacts = context.catalog->Query(node.op_type(), dtype, layout, capability);
+    std::string default_kernel;  // kernel_id of the op's default variant, matching or not
+    for (const KernelArtifact* artifact : artifacts) {
+      if (artifact->is_default) default_kernel = artifact->kernel_id;
+    }
+    std::vector<std::string> kernel_ids;
+    for (const KernelArtifact* artifact : artifacts) {
       if (!ArtifactMatches(*artifact, node, lookup, capability)) continue;
       ExecutionCandidate candidate;
       candidate.candidate_id = artifact->identity();
       candidate.is_default = artifact->is_default;
       candidate.steps.push_back(KernelInvocation{*artifact, node.inputs(), node.outputs()});
       candidates->push_back(std::move(candidate));
+      kernel_ids.push_back(artifact->kernel_id);
     }
-    // Without a matching default variant the first matching one leads.
+    // Without a matching default variant, another variant of the default
+    // kernel leads (a shape-specialised default falls back to its general
+    // sibling); failing that, the first matching candidate.
     if (!candidates->empty() &&
         std::none_of(candidates->begin(), candidates->end(),
                      [](const ExecutionCandidate& c) { return c.is_default; })) {
-      candidates->front().is_default = true;
+      std::size_t lead = 0;
+      for (std::size_t i = 0; i < kernel_ids.size(); ++i) {
+        if (!default_kernel.empty() && kernel_ids[i] == default_kernel) {
+          lead = i;
+          break;
+        }
+      }
+      (*candidates)[lead].is_default = true;
     }
     CUTRITON_RETURN_IF_ERROR(RegisterBuiltinFusionAlternatives());
     for (const auto& alternative : FusionRegistry::Global().Find(node.op_type())) {

@@ -61,19 +61,51 @@ constexpr int kGroupThreads = 128;    // four warps, one per lane quarter
 constexpr int kBoxRows = 64;          // weight rows (output channels) per TMA box
 constexpr uint32_t kBoxBytes = kBoxRows * kBK * 4;  // 8 KB
 constexpr uint32_t kTmemCols = 512;
+// Pipeline depths (compile-time; the pack's shared-memory size follows them).
+#ifndef CTB_TM_STAGES_N128
+#define CTB_TM_STAGES_N128 4
+#endif
+#ifndef CTB_TM_STAGES_N64
+#define CTB_TM_STAGES_N64 6
+#endif
+#ifndef CTB_TM_SLOTS
+#define CTB_TM_SLOTS 6
+#endif
+#ifndef CTB_TM_LOAD_AHEAD
+#define CTB_TM_LOAD_AHEAD 4
+#endif
+// 1 (the 1x1 variant): 1x1 / stride-1 / unpadded convolutions load each k
+// block of a tile that lies in one image with one TMA tensor copy ({128
+// pixels, 32 channels} of the [N][C][H*W] view) into a shared-memory ring;
+// the gather warps read it from there instead of issuing 32 global loads per
+// pixel. Other tiles and shapes use the global-load gather.
+#ifndef CTB_TM_A_TMA
+#define CTB_TM_A_TMA 0
+#endif
 constexpr int kMaxStages = 6;
-constexpr uint32_t kStageRegionBytes = 131072;      // max over configurations
+constexpr uint32_t kStageRegionBytes =
+    CTB_TM_STAGES_N128 * 32768 > CTB_TM_STAGES_N64 * 16384 ? CTB_TM_STAGES_N128 * 32768 : CTB_TM_STAGES_N64 * 16384;
 constexpr int kChunkTable = 256;                     // 4-wide k chunks described in shared memory
 // Epilogue staging ring: kSlots slots of [32 channels][128 pixels] FP32; the
 // residual is loaded kLoadAhead chunks ahead, so a slot is refilled two
 // chunks after its store was issued.
-constexpr int kSlots = 6;
-constexpr int kLoadAhead = 4;
+constexpr int kSlots = CTB_TM_SLOTS;
+constexpr int kLoadAhead = CTB_TM_LOAD_AHEAD;
+static_assert(kSlots <= 6 && kLoadAhead < kSlots && kSlots >= 4, "staging ring");
 constexpr uint32_t kStagingBytes = kSlots * 32 * 128 * 4;
+// Activation blocks in flight (1x1 variant). Even, so each slot is only ever
+// used by one gather group (items alternate between the two groups): a group
+// then waits on a slot's phases strictly in order. With an odd ring the other
+// group could reach a slot's next use while its current phase is still open,
+// and a parity wait would mistake the previous completed phase for it.
+constexpr int kARing = 4;
+static_assert(kARing % 2 == 0, "activation ring slots must belong to one gather group");
+constexpr uint32_t kARingBytes = CTB_TM_A_TMA ? kARing * 32 * 128 * 4 : 0;
 
 template <int BN>
 struct Tile {
-  static constexpr int kStages = BN == 64 ? 6 : 4;
+  static constexpr int kStages = BN == 64 ? CTB_TM_STAGES_N64 : CTB_TM_STAGES_N128;
+  static_assert(kStages <= kMaxStages, "stage count");
   static constexpr uint32_t kPlaneBytes = BN * kBK * 4;  // one of hi / lo
   static constexpr uint32_t kStageBytes = 2 * kPlaneBytes;
   static constexpr uint32_t kAColumn0 = 2 * BN;          // first activation stage column
@@ -94,12 +126,15 @@ struct __align__(8) Barriers {
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t residual_full[6];  // bulk residual loads, one per staging slot
+  uint64_t a_full[kARing];    // activation ring (1x1 variant): TMA landed / no-copy arrival
+  uint64_t a_empty[kARing];   // activation ring: the gather group has read the block
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
   int consumed;
 };
-static_assert(sizeof(Barriers) <= 256, "barrier block");
+constexpr uint32_t kBarrierBytes = 512;
+static_assert(sizeof(Barriers) <= kBarrierBytes, "barrier block");
 
 // 32 lanes x 32 consecutive 32-bit columns from registers: thread t of the
 // warp writes row (lane base + t).
@@ -235,7 +270,8 @@ __device__ __forceinline__ void gather_block(const PixelSource& px, const ConvSh
 
 template <int kEpilogue, int BN>
 __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_w, const TmaDescriptor* tma_out,
-                                        const TmaDescriptor* tma_res, const float* __restrict__ x,
+                                        const TmaDescriptor* tma_res, const TmaDescriptor* tma_x,
+                                        const float* __restrict__ x,
                                         const float* __restrict__ scale, const float* __restrict__ bias,
                                         const float* __restrict__ mean, const float* __restrict__ variance,
                                         const float* __restrict__ residual, float* __restrict__ out,
@@ -243,8 +279,9 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
   using T = Tile<BN>;
   constexpr int kStages = T::kStages;
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kStageRegionBytes);
-  int* chunk_table = reinterpret_cast<int*>(smem + kStageRegionBytes + 256);
-  float* staging = reinterpret_cast<float*>(smem + kStageRegionBytes + 256 + kChunkTable * 4);
+  int* chunk_table = reinterpret_cast<int*>(smem + kStageRegionBytes + kBarrierBytes);
+  float* staging = reinterpret_cast<float*>(smem + kStageRegionBytes + kBarrierBytes + kChunkTable * 4);
+  float* a_ring = staging + kStagingBytes / 4;
   volatile int* abort = &bars->abort;
   auto b_hi = [&](int s) { return smem + s * T::kStageBytes; };
   auto b_lo = [&](int s) { return smem + s * T::kStageBytes + T::kPlaneBytes; };
@@ -259,6 +296,20 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
   const int co_tiles = (p.k + BN - 1) / BN;
   const long long tiles = ((total_pixels + kBM - 1) / kBM) * co_tiles;
   const int my_tiles = tiles > blockIdx.x ? static_cast<int>((tiles - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+  // 1x1 variant: tiles of a 1x1 / stride-1 / unpadded convolution that lie in
+  // one image take their activation blocks by TMA (tma_x is encoded exactly
+  // when the planes are 16-byte aligned, which a_tma_shape checks too).
+  const bool a_tma_shape = CTB_TM_A_TMA && p.r == 1 && p.s == 1 && p.stride_h == 1 && p.stride_w == 1 &&
+                           p.pad_h == 0 && p.pad_w == 0 && p.c % kBK == 0 && (p.h * p.w) % 4 == 0 &&
+                           (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  auto tile_a_tma = [&](long long tile, int* hw0, int* img) {
+    if (!a_tma_shape) return false;
+    const long long p0 = (tile / co_tiles) * kBM;
+    const long long im = p0 / pixels_per_image;
+    *hw0 = static_cast<int>(p0 - im * pixels_per_image);
+    *img = static_cast<int>(im);
+    return *hw0 + min(static_cast<long long>(kBM), total_pixels - p0) <= pixels_per_image;
+  };
   // Bulk / tensor-copy epilogue: needs 16-byte aligned rows of every channel
   // plane, the same condition under which the host encodes tma_out / tma_res
   // (otherwise they are bound as zeros and must not be touched).
@@ -276,11 +327,16 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       mbar_init(&bars->tmem_empty[b], 4);
     }
     for (int b = 0; b < kSlots; ++b) mbar_init(&bars->residual_full[b], 32);  // 8 issuing lanes x 4 warps
+    for (int b = 0; b < kARing; ++b) {
+      mbar_init(&bars->a_full[b], 1);
+      mbar_init(&bars->a_empty[b], kGroupThreads);
+    }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
     bars->consumed = 0;
     mbar_init_fence();
     tma_prefetch(tma_w);
+    if (a_tma_shape) tma_prefetch(tma_x);
     if (bulk_epilogue) {
       tma_prefetch(tma_out);
       if (kEpilogue == kBatchNormAddRelu) tma_prefetch(tma_res);
@@ -309,6 +365,8 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       const int local = item / k_blocks;
       const int kb = item - local * k_blocks;
       const long long tile = blockIdx.x + static_cast<long long>(local) * gridDim.x;
+      int hw0, img;
+      if (tile_a_tma(tile, &hw0, &img)) return;  // arrives by TMA; read in publish
       const PixelSource px =
           pixel_source(x, p, (tile / co_tiles) * kBM + row, total_pixels, pixels_per_image);
       gather_block(px, p, cp, kdim, plane, kb, use_table ? chunk_table : nullptr, v);
@@ -316,6 +374,19 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     // Splits one block into hi / lo and writes it to the stage's TMEM columns.
     // Returns false when the kernel is aborting.
     auto publish = [&](int item, float (&v)[kBK]) -> bool {
+      if (CTB_TM_A_TMA) {
+        // Activation ring: every item passes through it (a no-copy arrival
+        // for items gathered from global memory) so its phases follow item.
+        const int sa = item % kARing;
+        if (!mbar_wait(&bars->a_full[sa], (item / kARing) & 1, abort, scratch, 40)) return false;
+        int hw0, img;
+        if (tile_a_tma(blockIdx.x + static_cast<long long>(item / k_blocks) * gridDim.x, &hw0, &img)) {
+          const float* blk = a_ring + sa * kBK * kBM + row;
+#pragma unroll
+          for (int kk = 0; kk < kBK; ++kk) v[kk] = blk[kk * kBM];
+        }
+        mbar_arrive(&bars->a_empty[sa]);
+      }
       const int s = item % kStages;
       const int use = item / kStages;
       if (use > 0 && !mbar_wait(&bars->empty[s], (use - 1) & 1, abort, scratch, 30)) return false;
@@ -356,6 +427,8 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     for (int local = 0; local < my_tiles && !stop; ++local) {
       const long long tile = blockIdx.x + static_cast<long long>(local) * gridDim.x;
       const int co0 = static_cast<int>(tile % co_tiles) * BN;
+      int a_hw0 = 0, a_img = 0;
+      const bool tile_uses_a_tma = tile_a_tma(tile, &a_hw0, &a_img);
       for (int kb = 0; kb < k_blocks; ++kb, ++g) {
         const int s = g % kStages;
         const int use = g / kStages;
@@ -369,6 +442,20 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
           tma_load_3d(b_hi(s) + b * kBoxBytes, tma_w, &bars->full_b[s], kb * kBK, co0 + b * kBoxRows, 0);
           tma_load_3d(b_lo(s) + b * kBoxBytes, tma_w, &bars->full_b[s], kb * kBK, co0 + b * kBoxRows, 1);
         }
+        if (CTB_TM_A_TMA) {
+          const int sa = g % kARing;
+          if (g >= kARing && !mbar_wait(&bars->a_empty[sa], (g / kARing - 1) & 1, abort, scratch, 41)) {
+            stop = true;
+            ++g;
+            break;
+          }
+          if (tile_uses_a_tma) {
+            mbar_arrive_expect_tx(&bars->a_full[sa], kBK * kBM * 4);
+            tma_load_3d(a_ring + sa * kBK * kBM, tma_x, &bars->a_full[sa], a_hw0, kb * kBK, a_img);
+          } else {
+            mbar_arrive(&bars->a_full[sa]);
+          }
+        }
       }
     }
     if (*abort) {
@@ -376,6 +463,13 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       for (int q = *reinterpret_cast<volatile int*>(&bars->consumed); q < g; ++q) {
         volatile int never = 0;
         mbar_wait(&bars->full_b[q % kStages], (q / kStages) & 1, &never, scratch, 32);
+      }
+      if (CTB_TM_A_TMA) {
+        // At most one activation copy per ring slot can be outstanding.
+        for (int q = max(0, g - kARing); q < g; ++q) {
+          volatile int never = 0;
+          mbar_wait(&bars->a_full[q % kARing], (q / kARing) & 1, &never, scratch, 42);
+        }
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -700,16 +794,17 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
 
 template <int kEpilogue>
 __device__ __forceinline__ void conv_tm_dispatch(const TmaDescriptor* tma_w, const TmaDescriptor* tma_out,
-                                                 const TmaDescriptor* tma_res, const float* x, const float* scale,
+                                                 const TmaDescriptor* tma_res, const TmaDescriptor* tma_x,
+                                                 const float* x, const float* scale,
                                                  const float* bias, const float* mean, const float* variance,
                                                  const float* residual, float* out, const ConvShape& p,
                                                  float epsilon, void* scratch) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   if (p.k <= 64) {
-    conv_tm<kEpilogue, 64>(smem, tma_w, tma_out, tma_res, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
+    conv_tm<kEpilogue, 64>(smem, tma_w, tma_out, tma_res, tma_x, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
   } else {
-    conv_tm<kEpilogue, 128>(smem, tma_w, tma_out, tma_res, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
+    conv_tm<kEpilogue, 128>(smem, tma_w, tma_out, tma_res, tma_x, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
   }
 }
 
@@ -723,37 +818,39 @@ __device__ __forceinline__ void conv_tm_dispatch(const TmaDescriptor* tma_w, con
 
 extern "C" __global__ void __launch_bounds__(kThreads, 1)
 ctb_conv_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const __grid_constant__ TmaDescriptor tma_out,
-                const float* x, float* output, CTB_CONV_DIMS, CTB_RESERVED_PARAMS) {
+                const __grid_constant__ TmaDescriptor tma_x, const float* x, float* output, CTB_CONV_DIMS,
+                CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kPlain>(&tma_w, &tma_out, nullptr, x, nullptr, nullptr, nullptr, nullptr, nullptr, output, CTB_CONV_SHAPE, 0.0f,
+  conv_tm_dispatch<kPlain>(&tma_w, &tma_out, nullptr, &tma_x, x, nullptr, nullptr, nullptr, nullptr, nullptr, output, CTB_CONV_SHAPE, 0.0f,
                            runtime_scratch);
 }
 
 extern "C" __global__ void __launch_bounds__(kThreads, 1)
 ctb_conv_bn_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const __grid_constant__ TmaDescriptor tma_out,
-                   const float* x, const float* scale, const float* bias, const float* mean, const float* variance,
+                   const __grid_constant__ TmaDescriptor tma_x, const float* x, const float* scale, const float* bias, const float* mean, const float* variance,
                    float* output, CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kBatchNorm>(&tma_w, &tma_out, nullptr, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE, epsilon,
+  conv_tm_dispatch<kBatchNorm>(&tma_w, &tma_out, nullptr, &tma_x, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE, epsilon,
                                runtime_scratch);
 }
 
 extern "C" __global__ void __launch_bounds__(kThreads, 1)
 ctb_conv_bn_relu_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const __grid_constant__ TmaDescriptor tma_out,
-                        const float* x, const float* scale, const float* bias, const float* mean,
+                        const __grid_constant__ TmaDescriptor tma_x, const float* x, const float* scale, const float* bias, const float* mean,
                         const float* variance, float* output, CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kBatchNormRelu>(&tma_w, &tma_out, nullptr, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE,
+  conv_tm_dispatch<kBatchNormRelu>(&tma_w, &tma_out, nullptr, &tma_x, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE,
                                    epsilon, runtime_scratch);
 }
 
 extern "C" __global__ void __launch_bounds__(kThreads, 1)
 ctb_conv_bn_add_relu_f32_tm(const __grid_constant__ TmaDescriptor tma_w,
                             const __grid_constant__ TmaDescriptor tma_out,
-                            const __grid_constant__ TmaDescriptor tma_res, const float* x, const float* scale,
+                            const __grid_constant__ TmaDescriptor tma_res,
+                            const __grid_constant__ TmaDescriptor tma_x, const float* x, const float* scale,
                             const float* bias, const float* mean, const float* variance, const float* residual,
                             float* output, CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kBatchNormAddRelu>(&tma_w, &tma_out, &tma_res, x, scale, bias, mean, variance, residual, output, CTB_CONV_SHAPE,
+  conv_tm_dispatch<kBatchNormAddRelu>(&tma_w, &tma_out, &tma_res, &tma_x, x, scale, bias, mean, variance, residual, output, CTB_CONV_SHAPE,
                                       epsilon, runtime_scratch);
 }

@@ -113,25 +113,47 @@ def _conv_specs() -> list[KernelSpec]:
     # tilings (64 when Cout <= 64, else 128).
     tma_w64 = arg("tma_w", "tensormap", "tensor_map", tensor="input", index=1, box=[32, 64, 1], swizzle=128,
                   prepack="conv_w_tf32x2_cb")
-    # weight stages + barriers + k-chunk table + epilogue staging ring + alignment slack
-    tm_smem = 131072 + 256 + 1024 + 6 * 16384 + 1024
+    def tm_smem(n128: int, n64: int, slots: int, a_ring: int) -> int:
+        # weight stages + barriers + k-chunk table + epilogue staging ring +
+        # activation ring + alignment slack
+        return max(n128 * 32768, n64 * 16384) + 512 + 1024 + slots * 16384 + a_ring * 16384 + 1024
+
+    def tm_defines(n128: int, n64: int, slots: int, ahead: int, a_tma: int) -> dict[str, str]:
+        return {"CTB_TM_STAGES_N128": str(n128), "CTB_TM_STAGES_N64": str(n64), "CTB_TM_SLOTS": str(slots),
+                "CTB_TM_LOAD_AHEAD": str(ahead), "CTB_TM_A_TMA": str(a_tma)}
+
     # Epilogue tensor copies over the [N][K][H*W] view (optional: bound as
     # zeros when H*W*4 is not a multiple of 16; the kernel then stores from
-    # registers).
+    # registers). tma_x: activation blocks of the 1x1 variant.
     tma_out = arg("tma_out", "tensormap", "tensor_map", tensor="output", index=0, box=[128, 32, 1], merge_inner=2,
                   optional=1)
     tma_res = arg("tma_res", "tensormap", "tensor_map", tensor="input", index=6, box=[128, 32, 1], merge_inner=2,
                   optional=1)
+    tma_x = arg("tma_x", "tensormap", "tensor_map", tensor="input", index=0, box=[128, 32, 1], merge_inner=2,
+                optional=1)
+    one_by_one = (
+        {"kind": "dim_le", "source": "input", "index": 1, "axis": 2, "value": 1},
+        {"kind": "dim_le", "source": "input", "index": 1, "axis": 3, "value": 1},
+        {"kind": "attribute_list_eq", "name": "strides", "value": [1, 1], "default": [1, 1]},
+        {"kind": "attribute_list_eq", "name": "pads", "value": [0, 0, 0, 0], "default": [0, 0, 0, 0]},
+    )
     for kernel_id, op_type, symbol, arguments in tc_families:
-        maps = (tma_w64, tma_out) + ((tma_res,) if op_type.endswith("AddRelu") else ())
+        maps = (tma_w64, tma_out) + ((tma_res,) if op_type.endswith("AddRelu") else ()) + (tma_x,)
         specs.append(KernelSpec(
             kernel_id=kernel_id.replace("tcgen05", "tcgen05_tmem"), op_type=op_type, version=1,
             source="conv_tm.cu", symbol=symbol.replace("_tc", "_tm"),
             arguments=maps + arguments[1:], grid=tc_grid, layout="NCHW",
             constraints=({"kind": "input_is_constant", "index": 1},),
-            variants=(Variant("persistent_m128n128k32_tmem_a_3xtf32", num_warps=14,
-                              shared_memory_bytes=tm_smem,
-                              meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, default=True),),
+            variants=(
+                # Any shape: activations gathered with global loads.
+                Variant("persistent_m128n128k32_tmem_a_3xtf32", num_warps=14,
+                        shared_memory_bytes=tm_smem(3, 6, 4, 0), defines=tm_defines(3, 6, 4, 2, 0),
+                        meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}),
+                # 1x1 / stride 1 / no padding: activation blocks by TMA.
+                Variant("persistent_m128n128k32_tmem_a_3xtf32_1x1tma", num_warps=14,
+                        shared_memory_bytes=tm_smem(3, 5, 4, 4), defines=tm_defines(3, 5, 4, 2, 1),
+                        meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, constraints=one_by_one, default=True),
+            ),
         ))
     for kernel_id, op_type, symbol, arguments in tc_families:
         stages = 3
