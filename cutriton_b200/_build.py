@@ -106,12 +106,15 @@ def compile_cubin(source: Path, output: Path, defines: dict[str, str] | None = N
     """``nvcc -cubin`` for sm_100a (with -lineinfo for profiler attribution)."""
     output.parent.mkdir(parents=True, exist_ok=True)
     deps = [source, *sorted((CSRC / "kernels").glob("*.cuh"))]
-    if _stale(output, deps):
-        flags = [f"-D{k}={v}" for k, v in (defines or {}).items()]
+    flags = [f"-D{k}={v}" for k, v in sorted((defines or {}).items())]
+    # The defines are part of the cubin's identity: a change rebuilds it.
+    stamp = output.with_suffix(".flags")
+    if _stale(output, deps) or not stamp.exists() or stamp.read_text() != " ".join(flags):
         tmp = output.with_suffix(".cubin.tmp")
         _run([str(NVCC), "-cubin", *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17",
               f"-I{CSRC / 'kernels'}", *flags, str(source), "-o", str(tmp)])
         os.replace(tmp, output)
+        stamp.write_text(" ".join(flags))
     return output
 
 

@@ -26,6 +26,7 @@
 // Persistent kernel: one CTA per SM walks the tiles (128 output pixels x BN
 // output channels, BN = 64 when Cout <= 64 else 128) in a static round-robin,
 // channel tile fastest so CTAs running together share activations in L2.
+// Pixel tiles are either flat over N*H*W or (1x1 variant) aligned to images.
 // TMEM (512 columns): two BN-column accumulators, then STAGES activation
 // stages of 64 columns (32 hi + 32 lo). Roles (14 warps):
 //   warp 0 lane 0 — TMA producer of the weight tiles, prepacked at engine
@@ -54,7 +55,14 @@ using namespace ctb::tc;
 
 constexpr int kBM = 128;  // output pixels per tile (TMEM lanes)
 constexpr int kBK = 32;   // k per block (128 bytes of FP32)
-constexpr int kThreads = 448;
+// Gather groups of four warps (one per TMEM lane quarter) taking k blocks in
+// turn: two when the blocks come from global loads, one suffices when they
+// arrive by TMA (and leaves 168 registers per thread instead of 128).
+#ifndef CTB_TM_GATHER_GROUPS
+#define CTB_TM_GATHER_GROUPS 2
+#endif
+constexpr int kGatherGroups = CTB_TM_GATHER_GROUPS;
+constexpr int kThreads = (6 + 4 * kGatherGroups) * 32;
 constexpr int kEpilogueWarp0 = 2;
 constexpr int kGatherWarp0 = 6;
 constexpr int kGroupThreads = 128;    // four warps, one per lane quarter
@@ -82,6 +90,12 @@ constexpr uint32_t kTmemCols = 512;
 #ifndef CTB_TM_A_TMA
 #define CTB_TM_A_TMA 0
 #endif
+// 1: pixel tiles never straddle images (ceil(H*W / 128) tiles per image, the
+// last one partly empty) whenever H*W is a multiple of 4, so every tile takes
+// the single-tensor-copy paths. 0: flat tiling over N*H*W pixels.
+#ifndef CTB_TM_IMAGE_TILES
+#define CTB_TM_IMAGE_TILES 0
+#endif
 constexpr int kMaxStages = 6;
 constexpr uint32_t kStageRegionBytes =
     CTB_TM_STAGES_N128 * 32768 > CTB_TM_STAGES_N64 * 16384 ? CTB_TM_STAGES_N128 * 32768 : CTB_TM_STAGES_N64 * 16384;
@@ -93,13 +107,13 @@ constexpr int kSlots = CTB_TM_SLOTS;
 constexpr int kLoadAhead = CTB_TM_LOAD_AHEAD;
 static_assert(kSlots <= 6 && kLoadAhead < kSlots && kSlots >= 4, "staging ring");
 constexpr uint32_t kStagingBytes = kSlots * 32 * 128 * 4;
-// Activation blocks in flight (1x1 variant). Even, so each slot is only ever
-// used by one gather group (items alternate between the two groups): a group
+// Activation blocks in flight (1x1 variant). A multiple of the gather group
+// count, so each slot is only ever used by one gather group: a group
 // then waits on a slot's phases strictly in order. With an odd ring the other
 // group could reach a slot's next use while its current phase is still open,
 // and a parity wait would mistake the previous completed phase for it.
 constexpr int kARing = 4;
-static_assert(kARing % 2 == 0, "activation ring slots must belong to one gather group");
+static_assert(kARing % kGatherGroups == 0, "activation ring slots must belong to one gather group");
 constexpr uint32_t kARingBytes = CTB_TM_A_TMA ? kARing * 32 * 128 * 4 : 0;
 
 template <int BN>
@@ -294,7 +308,20 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
   const long long pixels_per_image = static_cast<long long>(p.out_h) * p.out_w;
   const long long total_pixels = pixels_per_image * p.n;
   const int co_tiles = (p.k + BN - 1) / BN;
-  const long long tiles = ((total_pixels + kBM - 1) / kBM) * co_tiles;
+  // Pixel tile mt covers flat pixels [tile_p0(mt), tile_p0(mt) + tile_rows(mt)).
+  const bool image_tiles = CTB_TM_IMAGE_TILES && pixels_per_image % 4 == 0;
+  const long long tiles_per_image = (pixels_per_image + kBM - 1) / kBM;
+  const long long m_tiles = image_tiles ? p.n * tiles_per_image : (total_pixels + kBM - 1) / kBM;
+  auto tile_p0 = [&](long long mt) -> long long {
+    if (!image_tiles) return mt * kBM;
+    const long long img = mt / tiles_per_image;
+    return img * pixels_per_image + (mt - img * tiles_per_image) * kBM;
+  };
+  auto tile_rows = [&](long long mt) -> int {
+    if (!image_tiles) return static_cast<int>(min(static_cast<long long>(kBM), total_pixels - mt * kBM));
+    return static_cast<int>(min(static_cast<long long>(kBM), pixels_per_image - (mt % tiles_per_image) * kBM));
+  };
+  const long long tiles = m_tiles * co_tiles;
   const int my_tiles = tiles > blockIdx.x ? static_cast<int>((tiles - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
   // 1x1 variant: tiles of a 1x1 / stride-1 / unpadded convolution that lie in
   // one image take their activation blocks by TMA (tma_x is encoded exactly
@@ -304,11 +331,11 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
                            (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   auto tile_a_tma = [&](long long tile, int* hw0, int* img) {
     if (!a_tma_shape) return false;
-    const long long p0 = (tile / co_tiles) * kBM;
+    const long long p0 = tile_p0(tile / co_tiles);
     const long long im = p0 / pixels_per_image;
     *hw0 = static_cast<int>(p0 - im * pixels_per_image);
     *img = static_cast<int>(im);
-    return *hw0 + min(static_cast<long long>(kBM), total_pixels - p0) <= pixels_per_image;
+    return *hw0 + tile_rows(tile / co_tiles) <= pixels_per_image;
   };
   // Bulk / tensor-copy epilogue: needs 16-byte aligned rows of every channel
   // plane, the same condition under which the host encodes tma_out / tma_res
@@ -368,7 +395,8 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       int hw0, img;
       if (tile_a_tma(tile, &hw0, &img)) return;  // arrives by TMA; read in publish
       const PixelSource px =
-          pixel_source(x, p, (tile / co_tiles) * kBM + row, total_pixels, pixels_per_image);
+          pixel_source(x, p, row < tile_rows(tile / co_tiles) ? tile_p0(tile / co_tiles) + row : total_pixels,
+                       total_pixels, pixels_per_image);
       gather_block(px, p, cp, kdim, plane, kb, use_table ? chunk_table : nullptr, v);
     };
     // Splits one block into hi / lo and writes it to the stage's TMEM columns.
@@ -412,13 +440,13 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     int item = group;
     if (item < items) fetch(item, buf_a);
     while (item < items) {
-      if (item + 2 < items) fetch(item + 2, buf_b);
+      if (item + kGatherGroups < items) fetch(item + kGatherGroups, buf_b);
       if (!publish(item, buf_a)) break;
-      item += 2;
+      item += kGatherGroups;
       if (item >= items) break;
-      if (item + 2 < items) fetch(item + 2, buf_a);
+      if (item + kGatherGroups < items) fetch(item + kGatherGroups, buf_a);
       if (!publish(item, buf_b)) break;
-      item += 2;
+      item += kGatherGroups;
     }
   } else if (warp == 0 && lane == 0) {
     // ---- TMA producer: weight hi / lo tiles ----
@@ -574,8 +602,8 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       // Calls fn(smem_offset_px, global_offset, pixels) for each run of
       // channel `ch` of tile `tile` (valid pixels only).
       auto for_each_run = [&](long long tile, int ch, auto&& fn) {
-        const long long p0 = (tile / co_tiles) * kBM;
-        const int n_valid = static_cast<int>(min(static_cast<long long>(kBM), total_pixels - p0));
+        const long long p0 = tile_p0(tile / co_tiles);
+        const int n_valid = tile_rows(tile / co_tiles);
         long long img = p0 / pixels_per_image;
         int hw = static_cast<int>(p0 - img * pixels_per_image);
         for (int pos = 0; pos < n_valid; ++img, hw = 0) {
@@ -594,10 +622,10 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         bool one_image;
       };
       auto span_of = [&](long long tile) {
-        const long long p0 = (tile / co_tiles) * kBM;
+        const long long p0 = tile_p0(tile / co_tiles);
         const long long img = p0 / pixels_per_image;
         const int hw0 = static_cast<int>(p0 - img * pixels_per_image);
-        const int n_valid = static_cast<int>(min(static_cast<long long>(kBM), total_pixels - p0));
+        const int n_valid = tile_rows(tile / co_tiles);
         return TileSpan{hw0, static_cast<int>(img), hw0 + n_valid <= pixels_per_image};
       };
       const bool leader = ew == 0 && lane == 0;  // issues the tensor copies
@@ -710,12 +738,13 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         if (local < my_tiles) {
           const long long tile = tile_index(local);
           const int ch_base = static_cast<int>(tile % co_tiles) * BN + 32 * ci;
-          const long long p0 = (tile / co_tiles) * kBM;
+          const long long p0 = tile_p0(tile / co_tiles);
+          const int rows = tile_rows(tile / co_tiles);
           float* slot = staging + ci * 32 * kBM;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const long long px = p0 + 32 * q + lane;
-            const bool pix_ok = px < total_pixels;
+            const bool pix_ok = 32 * q + lane < rows;
             long long src0 = 0;
             if (pix_ok) {
               const long long img = px / pixels_per_image;
@@ -741,8 +770,8 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         const int buf = local & 1;
         const long long tile = tile_index(local);
         const int co0 = static_cast<int>(tile % co_tiles) * BN;
-        const long long pixel = (tile / co_tiles) * kBM + quarter * 32 + lane;
-        const bool valid = pixel < total_pixels;
+        const long long pixel = tile_p0(tile / co_tiles) + quarter * 32 + lane;
+        const bool valid = quarter * 32 + lane < tile_rows(tile / co_tiles);
         long long base = 0;  // output offset of (image, channel 0, pixel)
         if (valid) {
           const long long img = pixel / pixels_per_image;

@@ -120,7 +120,8 @@ def _conv_specs() -> list[KernelSpec]:
 
     def tm_defines(n128: int, n64: int, slots: int, ahead: int, a_tma: int) -> dict[str, str]:
         return {"CTB_TM_STAGES_N128": str(n128), "CTB_TM_STAGES_N64": str(n64), "CTB_TM_SLOTS": str(slots),
-                "CTB_TM_LOAD_AHEAD": str(ahead), "CTB_TM_A_TMA": str(a_tma)}
+                "CTB_TM_LOAD_AHEAD": str(ahead), "CTB_TM_A_TMA": str(a_tma), "CTB_TM_IMAGE_TILES": "0",
+                "CTB_TM_GATHER_GROUPS": "2"}
 
     # Epilogue tensor copies over the [N][K][H*W] view (optional: bound as
     # zeros when H*W*4 is not a multiple of 16; the kernel then stores from
@@ -136,6 +137,9 @@ def _conv_specs() -> list[KernelSpec]:
         {"kind": "dim_le", "source": "input", "index": 1, "axis": 3, "value": 1},
         {"kind": "attribute_list_eq", "name": "strides", "value": [1, 1], "default": [1, 1]},
         {"kind": "attribute_list_eq", "name": "pads", "value": [0, 0, 0, 0], "default": [0, 0, 0, 0]},
+        # even H and W: H*W % 4 == 0, so every image-aligned tile moves by tensor copies
+        {"kind": "dim_multiple_of", "source": "output", "index": 0, "axis": 2, "value": 2},
+        {"kind": "dim_multiple_of", "source": "output", "index": 0, "axis": 3, "value": 2},
     )
     for kernel_id, op_type, symbol, arguments in tc_families:
         maps = (tma_w64, tma_out) + ((tma_res,) if op_type.endswith("AddRelu") else ()) + (tma_x,)
