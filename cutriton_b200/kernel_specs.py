@@ -299,7 +299,7 @@ def _gemm_specs() -> list[KernelSpec]:
 
     def tc_variants() -> tuple[Variant, ...]:
         out = []
-        for block_n, stages, default in ((128, 4, True), (128, 3, False), (256, 3, False)):
+        for block_n, stages, default in ((128, 4, False), (128, 3, False), (256, 3, False)):
             smem = stages * (128 * 64 * 2 + block_n * 64 * 2) + 1024 + 256
             out.append(Variant(f"m128n{block_n}k64s{stages}", num_warps=4, shared_memory_bytes=smem,
                                meta={"BLOCK_M": 128, "BLOCK_N": block_n},
@@ -307,7 +307,29 @@ def _gemm_specs() -> list[KernelSpec]:
                                arg_overrides={"tma_b": {"box": [64, block_n]}}))
         return tuple(out)
 
+    # Persistent: min(#128x128 tiles, #SMs) CTAs; the kernel picks 256- or
+    # 128-wide tiles at run time.
+    tp_args = (
+        arg("tma_a", "tensormap", "tensor_map", tensor="input", index=0, box=[64, 128], swizzle=128),
+        arg("tma_b", "tensormap", "tensor_map", tensor="input", index=1, box=[64, 128], swizzle=128,
+            prepack="transpose_2d"),
+        arg("tma_out", "tensormap", "tensor_map", tensor="output", index=0, box=[64, 32], swizzle=128, optional=1),
+        arg("output", "*fp16", "output", index=0),
+        arg("m", "i32", "output_dim", index=0, axis=0),
+        arg("n", "i32", "output_dim", index=0, axis=1),
+        arg("k", "i32", "input_dim", index=0, axis=1),
+    ) + RESERVED
+    tp_grid = ({"kind": "min", "args": [mul(ceil_div(out_dim(0), meta("BLOCK_M")), ceil_div(out_dim(1), meta("BLOCK_N"))),
+                                        {"kind": "sm_count"}]},)
+    tp_variant = Variant("persistent_m128n256k64_2acc", num_warps=6, shared_memory_bytes=196608 + 32768 + 256 + 1024,
+                         meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=True)
     tc = [
+        KernelSpec(kernel_id="gemm.fp16.tcgen05_persistent", op_type="Gemm", version=1, source="gemm_f16_tp.cu",
+                   symbol="ctb_gemm_f16_tp", arguments=tp_args, grid=tp_grid, dtype="float16",
+                   constraints=tc_constraints, variants=(tp_variant,)),
+        KernelSpec(kernel_id="gemm_gelu.fp16.tcgen05_persistent", op_type="GemmGelu", version=1,
+                   source="gemm_f16_tp.cu", symbol="ctb_gemm_gelu_f16_tp", arguments=tp_args, grid=tp_grid,
+                   dtype="float16", constraints=tc_constraints, variants=(tp_variant,)),
         KernelSpec(kernel_id="gemm.fp16.tcgen05", op_type="Gemm", version=1, source="gemm_f16_tc.cu",
                    symbol="ctb_gemm_f16_tc", arguments=tc_args(128), grid=grid, dtype="float16",
                    constraints=tc_constraints, variants=tc_variants()),

@@ -180,7 +180,9 @@ def test_gemm_f32(cuda, mnk):
         assert_close(out["y"], expected, atol=tol, rtol=tol, what=f"Gemm f32 {cand}")
 
 
-@pytest.mark.parametrize("mnk", [(256, 3072, 768), (17, 512, 128), (128, 768, 3072), (33, 200, 72)])
+@pytest.mark.parametrize("mnk", [(256, 3072, 768), (17, 512, 128), (128, 768, 3072), (33, 200, 72),
+                                 # persistent kernel: >1 tile per CTA with 128-wide tiles, and 256-wide tiles
+                                 (1280, 2560, 64), (2048, 4864, 128)])
 @pytest.mark.parametrize("op", ["Gemm", "GemmGelu"])
 def test_gemm_f16(cuda, mnk, op):
     m, n, k = mnk
