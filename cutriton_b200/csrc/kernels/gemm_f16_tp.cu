@@ -1,7 +1,7 @@
 // Persistent FP16 GEMM / GEMM+GELU on the 5th-generation tensor cores.
 //
 // C[M,N] = A[M,K] . B[K,N] (FP16 in, FP32 accumulate in TMEM, optional
-// exact-erf GELU, round-to-nearest FP16 out) — the math of
+// erf-GELU (erf to 1.5e-7, common.cuh), round-to-nearest FP16 out) — the math of
 // python/cutriton/triton_kernels/transformer.py:17-107. B is a constant
 // weight prepacked once to B^T [N, K] ("transpose_2d"), so both operands are
 // K-major and staged by TMA in the 128-byte-swizzled layout the UMMA
@@ -9,17 +9,18 @@
 //
 // One CTA per SM walks the 128 x BN output tiles (BN = 256, or 128 when
 // 256-wide tiles would leave SMs idle) in a static round-robin, N fastest so
-// co-running CTAs share the A tile in L2. Roles (6 warps):
+// co-running CTAs share the A tile in L2. Roles (10 warps):
 //   warp 0 lane 0 — TMA producer: A (128 x 64) and B (BN x 64) per k block
 //       through a STAGES-deep shared-memory ring (full / empty barriers);
 //   warp 1 lane 0 — UMMA issuer: 4 x (128 x BN x 16) per k block into one of
 //       two TMEM accumulators (2 x BN columns), so the epilogue of one tile
 //       overlaps the MMAs of the next;
-//   warps 2-5 — epilogue, TMEM lane quarter (warp % 4) = 32 rows: 64 columns
-//       at a time -> GELU -> FP16 -> a 32 x 64 staging box in shared memory
-//       (128-byte swizzle, conflict-free 16-byte writes) -> TMA tensor store,
-//       double-buffered per warp; the accumulator is handed back as soon as
-//       its last columns are in registers.
+//   warps 2-9 — epilogue, two warps per TMEM lane quarter (warp % 4 = 32
+//       rows), each taking half of the columns, 64 at a time -> GELU -> FP16
+//       -> a 32 x 64 staging box in shared memory (128-byte swizzle,
+//       conflict-free 16-byte writes) -> TMA tensor store; each warp hands its
+//       half of the accumulator back as soon as it is in registers. Eight
+//       warps keep the erf-GELU of one tile shorter than the next tile's MMAs.
 // All waits are bounded (tc_common.cuh).
 
 #include "tc_common.cuh"
@@ -30,13 +31,14 @@ using namespace ctb::tc;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // FP16 elements per 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEpilogueWarps = 8;
 constexpr int kEpilogueWarp0 = 2;
 constexpr uint32_t kTileA = kBM * kBK * 2;      // 16 KB
 constexpr uint32_t kBoxRowsB = 128;              // B rows (N) per TMA box
 constexpr uint32_t kRingBytes = 196608;          // 4 x (16 + 32) KB = 6 x (16 + 16) KB
 constexpr uint32_t kStageBoxBytes = 32 * 128;    // 32 rows x 64 FP16 (one store box)
-constexpr uint32_t kStagingBytes = 4 * 2 * kStageBoxBytes;
+constexpr uint32_t kStagingBytes = kEpilogueWarps * kStageBoxBytes;
 constexpr int kMaxStages = 6;
 
 template <int BN>
@@ -94,7 +96,7 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->tmem_full[b], 1);
-      mbar_init(&bars->tmem_empty[b], 4);
+      mbar_init(&bars->tmem_empty[b], kEpilogueWarps);
     }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
@@ -178,10 +180,11 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
       mbar_wait(&bars->drain, 0, &never, scratch, 54);
     }
   } else if (warp >= kEpilogueWarp0) {
-    // ---- epilogue: rows quarter*32 + lane of each tile ----
+    // ---- epilogue: rows quarter*32 + lane, columns [c_begin, c_begin + BN/2) ----
     const int quarter = warp & 3;
-    uint8_t* boxes = staging + (warp - kEpilogueWarp0) * 2 * kStageBoxBytes;
-    int box_use = 0;  // stores issued by this warp (alternating staging boxes)
+    const int c_begin = ((warp - kEpilogueWarp0) / 4) * (BN / 2);
+    uint8_t* box = staging + (warp - kEpilogueWarp0) * kStageBoxBytes;
+    bool box_used = false;
     for (int local = 0; local < my_tiles; ++local) {
       const int buf = local & 1;
       const int tile = blockIdx.x + local * gridDim.x;
@@ -194,12 +197,12 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
       const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
       const int row = m0 + quarter * 32 + lane;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 64) {
+      for (int c = c_begin; c < c_begin + BN / 2; c += 64) {
         uint32_t v[64];
         tmem_load_32x32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         tmem_load_32x32(taddr + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-        if (c + 64 == BN) {
-          // Every column of the accumulator is in registers: hand it back.
+        if (c + 64 == c_begin + BN / 2) {
+          // This warp's columns of the accumulator are in registers: hand them back.
           tc_fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
@@ -213,17 +216,16 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
             float a = __uint_as_float(v[ch * 8 + 2 * j]);
             float b = __uint_as_float(v[ch * 8 + 2 * j + 1]);
             if (kGelu) {
-              a = ctb::gelu_erf(a);
-              b = ctb::gelu_erf(b);
+              a = ctb::gelu_erf_fast(a);
+              b = ctb::gelu_erf_fast(b);
             }
             h[j] = __floats2half2_rn(a, b);
           }
         }
         if (tma_epilogue) {
-          uint8_t* box = boxes + (box_use & 1) * kStageBoxBytes;
-          if (box_use >= 2) {
-            // The store issued from this box two boxes ago has read it out.
-            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          if (box_used) {
+            // The previous store from this box has read it out.
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             __syncwarp();
           }
           // Row `lane` (128 bytes), 16-byte chunk j at chunk j ^ (lane % 8).
@@ -237,7 +239,7 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
             tma_store_2d(tma_out, box, n0 + c, m0 + quarter * 32);
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
-          ++box_use;
+          box_used = true;
         } else if (row < m) {
           __half* dst = out + static_cast<long long>(row) * n + n0 + c;
 #pragma unroll

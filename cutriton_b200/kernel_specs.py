@@ -321,7 +321,7 @@ def _gemm_specs() -> list[KernelSpec]:
     ) + RESERVED
     tp_grid = ({"kind": "min", "args": [mul(ceil_div(out_dim(0), meta("BLOCK_M")), ceil_div(out_dim(1), meta("BLOCK_N"))),
                                         {"kind": "sm_count"}]},)
-    tp_variant = Variant("persistent_m128n256k64_2acc", num_warps=6, shared_memory_bytes=196608 + 32768 + 256 + 1024,
+    tp_variant = Variant("persistent_m128n256k64_2acc", num_warps=10, shared_memory_bytes=196608 + 32768 + 256 + 1024,
                          meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=True)
     tc = [
         KernelSpec(kernel_id="gemm.fp16.tcgen05_persistent", op_type="Gemm", version=1, source="gemm_f16_tp.cu",
