@@ -38,6 +38,7 @@ sys.path.insert(0, str(REPO))
 PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 RN_BATCH_PER_GPU = 256
+UNFUSED = "unfused:"  # candidate-id prefix of the unfused decompositions
 FFN = dict(tokens=4096, hidden=768, inner=3072)
 
 
@@ -53,6 +54,9 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
                    help="run one small kernel case three times (for ncu captures) and exit")
+    p.add_argument("--config", type=int, choices=[2, 3, 4],
+                   help="2: dynamic-batch ResNet-50 (profile 1/32/128, graph LRU 4, TuneOnMiss); "
+                        "3: per-layer conv sweep at N=256; 4: FFN H=1024 I=4096 M=65536 (sharded over ranks)")
     return p.parse_args()
 
 
@@ -125,6 +129,134 @@ def run_profile_case(name: str) -> None:
         ctx.run()
     torch.cuda.synchronize()
     print(json.dumps({"profile_case": name, "runs": 3}), flush=True)
+
+
+def conv_shapes() -> list[tuple[int, int, int, int, int, int]]:
+    """Distinct ResNet-50 conv shapes (cin, cout, kernel, stride, pad, input H=W), in network order."""
+    from cutriton_b200 import workloads
+
+    shapes, h, block_in = [], 224, 224
+    for kind, item in workloads.resnet50_layers():
+        if kind == "maxpool":
+            h = (h + 2 - 3) // 2 + 1
+            block_in = h
+            continue
+        if kind == "block_add":
+            block_in = h
+            continue
+        ih = block_in if item.prefix.endswith(("_conv1", "_downsample")) else h
+        key = (item.cin, item.cout, item.kernel, item.stride, item.pad, ih)
+        if key not in shapes:
+            shapes.append(key)
+        if not item.prefix.endswith("_downsample"):
+            h = (ih + 2 * item.pad - item.kernel) // item.stride + 1
+    return shapes
+
+
+def time_context(ctx, stream, steps: int, warmup: int) -> float:
+    """Median ms of `steps` RunAsync calls timed with CUDA events on `stream`."""
+    import torch
+
+    for _ in range(max(3, warmup)):
+        ctx.run_async(stream.cuda_stream)
+        ctx.synchronize()
+    times = []
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ctx.run_async(stream.cuda_stream)
+        b.record(stream)
+        ctx.synchronize()
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    return float(np.median(times))
+
+
+def run_config2(args, tuning: str = "TuneOnMiss") -> dict:
+    """Config 2: one engine with a dynamic batch profile min/opt/max = 1/32/128, a CUDA-graph LRU of
+    capacity 4 and the tuner in TuneOnMiss mode (fused vs unfused candidates), run at 32, 64, 128."""
+    import tempfile
+
+    import torch
+    import cutriton_b200 as ct
+    from cutriton_b200 import workloads
+
+    weights = workloads.resnet50_weights("baseline", seed=0)
+    model = workloads.build_resnet50(weights, dynamic_batch=True)
+    model.add_shape_profile("batch", "input", [1, 3, 224, 224], [32, 3, 224, 224], [128, 3, 224, 224])
+    cache = tempfile.mkdtemp(prefix="ctb_tuning_")
+    mode = ct.TUNING_TUNE_ON_MISS if tuning == "TuneOnMiss" else ct.TUNING_DISABLED
+    engine = ct.build_engine(model, enable_cuda_graph=True, enable_residual_fusion=True,
+                             tuning_mode=mode, tuning_cache_dir=cache, cuda_graph_cache_capacity=4)
+    ctx = engine.create_context()
+    stream = torch.cuda.Stream()
+    results = {}
+    for batch in (32, 64, 128):
+        ctx.set_input_shape("input", [batch, 3, 224, 224])
+        ctx.resolve_shapes()
+        x = torch.from_numpy(workloads.resnet50_input(batch, seed=0)).cuda()
+        y = torch.empty(batch, 1000, device="cuda")
+        ctx.bind_tensor("input", x)
+        ctx.bind_tensor("output", y, output=True)
+        ms = time_context(ctx, stream, args.steps, args.warmup)
+        results[str(batch)] = {"ms": ms, "img_s": batch / ms * 1e3}
+    ops = engine.ops()
+    chosen = [op["candidates"][ctx.selected_candidate(i)] for i, op in enumerate(ops)]
+    unfused = sum(1 for c in chosen if c.startswith(UNFUSED))
+    kinds: dict[str, int] = {}
+    for c in chosen:
+        kind = c.split(":")[1] if ":" in c else c
+        kinds[kind] = kinds.get(kind, 0) + 1
+    return {"metric": "ResNet-50 FP32 img/s, dynamic batch profile (config 2)", "unit": "img/s",
+            "higher_is_better": True, "config": {"workload": "resnet50_dynamic_batch", "profile": [1, 32, 128],
+                                                "graph_lru": 4, "tuning": tuning},
+            "batches": results, "cached_graphs": ctx.cached_graph_count(), "ops": engine.num_ops(),
+            "ops_tuned_to_unfused": unfused, "selected_kernels": kinds}
+
+
+def run_config3(args, peaks) -> dict:
+    """Config 3: one FusedConvBatchNormRelu graph per distinct ResNet-50 conv shape at N=256."""
+    import torch
+
+    peak_tf = peaks["bf16_tflops_sustained"] / 6.0
+    rows = []
+    for cin, cout, kernel, stride, pad, h in conv_shapes():
+        e, ctx, keep = _conv_case(256, cin, h, cout, kernel, stride, pad)
+        ms = time_context(ctx, torch.cuda.Stream(), args.steps, args.warmup)
+        ho = (h + 2 * pad - kernel) // stride + 1
+        flops = 2.0 * 256 * ho * ho * cout * cin * kernel * kernel
+        nbytes = 4.0 * 256 * (cin * h * h + cout * ho * ho)
+        rows.append({"shape": f"{cin}->{cout} k{kernel} s{stride} {h}x{h}", "ms": round(ms, 4),
+                     "tflops": round(flops / ms / 1e9, 1), "tensor_frac": round(flops / ms / 1e9 / peak_tf, 3),
+                     "gbs": round(nbytes / ms / 1e6, 1), "hbm_frac": round(nbytes / ms / 1e6 / peaks["hbm_gbs"], 3),
+                     "candidate": e.ops()[0]["candidates"][ctx.selected_candidate(0)]})
+        del ctx, e, keep
+    return {"metric": "per-layer FusedConvBatchNormRelu sweep, N=256 (config 3)", "unit": "TFLOP/s",
+            "peak_basis": f"3xTF32 = bf16_tflops_sustained / 6 = {peak_tf:.1f} TFLOP/s; HBM {peaks['hbm_gbs']} GB/s",
+            "layers": rows}
+
+
+def run_config4(args, world, rank, local) -> dict:
+    """Config 4: FFN H=1024, I=4096, global M=65536 split over the ranks (no collective)."""
+    import torch
+    import cutriton_b200 as ct
+    from cutriton_b200 import workloads
+
+    h, i, global_m = 1024, 4096, 65536
+    m_rank = global_m // world
+    w = workloads.ffn_weights(h, i, seed=0)
+    engine = ct.build_engine(workloads.build_ffn(w, m_rank, h, i), device_id=local, enable_cuda_graph=True,
+                             tuning_mode=ct.TUNING_DISABLED)
+    ctx = engine.create_context()
+    x = torch.from_numpy(workloads.ffn_input(m_rank, h, seed=rank)).cuda(local)
+    y = torch.empty(m_rank, h, dtype=torch.float16, device=f"cuda:{local}")
+    ctx.bind_tensor("x", x)
+    ctx.bind_tensor("output", y, output=True)
+    ms = max_over_ranks(time_context(ctx, torch.cuda.Stream(local), args.steps, args.warmup), world)
+    flops = 4.0 * h * i * global_m
+    return {"metric": "FFN FP16 tokens/s (config 4: H=1024, I=4096, global M=65536)", "unit": "tokens/s",
+            "value": global_m / ms * 1e3, "ms_per_step": ms, "tflops": flops / ms / 1e9, "n_gpus": world,
+            "scaling": "strong", "higher_is_better": True}
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -468,6 +600,21 @@ def main() -> None:
 
     world, rank, local = dist_setup(args)
     peaks, peak_kind = load_peaks()
+    if args.config is not None:
+        if args.config == 4:
+            line = run_config4(args, world, rank, local)
+        elif rank == 0:
+            line = run_config2(args) if args.config == 2 else run_config3(args, peaks)
+        else:
+            line = None
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     rn = run_resnet(args, world, rank, local, peaks, peak_kind)
     ffn = None if args.no_ffn else run_ffn(args, world, rank, local)
     if rank == 0:

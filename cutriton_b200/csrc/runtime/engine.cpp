@@ -680,7 +680,14 @@ Status ExecutionContext::PrepareTuning() {
     double best_ms = std::numeric_limits<double>::infinity();
     std::size_t best = op.selected_candidate;
     std::vector<float> reference;
+    // The default candidate runs first and is the numerical reference (it is
+    // always eligible); intermediate inputs may hold anything during tuning,
+    // so elements where it is not finite are not compared.
+    std::vector<std::size_t> order{op.selected_candidate};
     for (std::size_t c = 0; c < op.candidates.size(); ++c) {
+      if (c != op.selected_candidate) order.push_back(c);
+    }
+    for (const std::size_t c : order) {
       std::vector<std::unique_ptr<OpKernel>> kernels;
       for (const auto& step : op.candidates[c].steps) {
         const auto* inv = std::get_if<KernelInvocation>(&step);
@@ -704,6 +711,7 @@ Status ExecutionContext::PrepareTuning() {
         const float rel = tensors_.at(op.outputs.front()).desc().dtype == DataType::kFloat16 ? 1e-2f : 1e-4f;
         bool same = true;
         for (std::size_t e = 0; e < produced.size() && same; ++e) {
+          if (!std::isfinite(reference[e])) continue;
           const float tol = rel + rel * std::fabs(reference[e]);
           same = std::isfinite(produced[e]) && std::fabs(produced[e] - reference[e]) <= tol;
         }
