@@ -506,6 +506,9 @@ Status RegisterBuiltinOpSchemas() {
   CUTRITON_RETURN_IF_ERROR(add("AveragePool", 1, 1, InferPool));
   CUTRITON_RETURN_IF_ERROR(add("GlobalAveragePool", 1, 1, InferGlobalAveragePool));
   CUTRITON_RETURN_IF_ERROR(add("Constant", 0, 0, [](Graph*, const Node&) { return Status::OK(); }));
+  // Diagnostic op of this backend: y = x after a bounded wait that always
+  // expires (exercises the kernel error block; see kernels/diag.cu).
+  CUTRITON_RETURN_IF_ERROR(add("BoundedWaitProbe", 1, 1, InferLikeFirstInput));
   return Status::OK();
 }
 

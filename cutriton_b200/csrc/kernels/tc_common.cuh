@@ -73,23 +73,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for phase `parity` of `bar` to complete. Returns false (after
-// recording the error) when the wait exceeds the limit or `abort` is set by
+// recording the error) when the wait exceeds `limit_ns` or `abort` is set by
 // another thread of the CTA.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, void* scratch,
-                                          unsigned int site) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort, void* scratch,
+                                              unsigned int site, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_time_ns();
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((spin & 255u) == 0) {
       if (*abort) return false;
-      if (global_time_ns() - start > kWaitLimitNs) {
+      if (global_time_ns() - start > limit_ns) {
         *abort = 1;
         report_error(scratch, kErrorWaitTimeout, site);
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, void* scratch,
+                                          unsigned int site) {
+  return mbar_wait_for(bar, parity, abort, scratch, site, kWaitLimitNs);
 }
 
 // ---- TMA ----------------------------------------------------------------------

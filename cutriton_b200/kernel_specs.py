@@ -398,5 +398,19 @@ def _norm_specs() -> list[KernelSpec]:
     ]
 
 
+def _diag_specs() -> list[KernelSpec]:
+    """Failure-detection probe: a bounded wait that always expires, then y = x."""
+    arguments = (
+        arg("x", "*fp32", "input", index=0),
+        arg("output", "*fp32", "output", index=0),
+        arg("numel", "i32", "input_numel", index=0),
+        arg("limit_us", "i32", "attribute_i64", name="limit_us", default=50000),
+    ) + RESERVED
+    return [KernelSpec(kernel_id="bounded_wait_probe.fp32", op_type="BoundedWaitProbe", version=1, source="diag.cu",
+                       symbol="ctb_bounded_wait_probe_f32", arguments=arguments,
+                       grid=({"kind": "min", "args": [ceil_div(out_numel(), literal(256)), literal(1024)]},),
+                       variants=(Variant("single_waiter", num_warps=8, default=True),))]
+
+
 def all_specs() -> list[KernelSpec]:
-    return [*_conv_specs(), *_elementwise_specs(), *_pool_specs(), *_gemm_specs(), *_norm_specs()]
+    return [*_conv_specs(), *_elementwise_specs(), *_pool_specs(), *_gemm_specs(), *_norm_specs(), *_diag_specs()]
