@@ -125,10 +125,29 @@ def build_pack(jobs: int = 8) -> Path:
     return kernel_sdk.build_pack(PACK_DIR, compile_cubin, jobs=jobs)
 
 
+NOALLOC_SOURCE = CSRC / "noalloc" / "gemm_f16_noalloc.cu"
+NOALLOC_LIBRARY = LIB_DIR / "libcutriton_b200_noalloc.so"
+
+
+def build_noalloc_library() -> Path:
+    """``libcutriton_b200_noalloc.so``: the no-allocation FP16 GEMM entry point
+    (CUDA runtime, static cudart; the kernel comes from kernels/gemm_f16_tp.cu)."""
+    LIB_DIR.mkdir(parents=True, exist_ok=True)
+    deps = [NOALLOC_SOURCE, CSRC / "kernels" / "gemm_f16_tp.cu", INCLUDE / "cutriton_b200_noalloc.h",
+            *sorted((CSRC / "kernels").glob("*.cuh"))]
+    if _stale(NOALLOC_LIBRARY, deps):
+        tmp = NOALLOC_LIBRARY.with_suffix(".so.tmp")
+        _run([str(NVCC), "-shared", "-Xcompiler", "-fPIC", *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17",
+              "-cudart", "static", f"-I{INCLUDE}", f"-I{CSRC / 'kernels'}", str(NOALLOC_SOURCE), "-o", str(tmp)])
+        os.replace(tmp, NOALLOC_LIBRARY)
+    return NOALLOC_LIBRARY
+
+
 def build_all(jobs: int | None = None) -> None:
     jobs = jobs or min(16, os.cpu_count() or 4)
     build_library(jobs)
     build_pack(jobs)
+    build_noalloc_library()
 
 
 if __name__ == "__main__":
