@@ -39,6 +39,7 @@ PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 RN_BATCH_PER_GPU = 256
 UNFUSED = "unfused:"  # candidate-id prefix of the unfused decompositions
+CONV_DRAM_BYTES_PER_STEP_BS256 = 26.110e9  # ncu, conv family, one bs256 step (see roofline.traffic)
 FFN = dict(tokens=4096, hidden=768, inner=3072)
 
 
@@ -462,7 +463,12 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
             "peak_basis": f"{peak_kind} bf16_tflops_sustained {peaks['bf16_tflops_sustained']} / 6 (3xTF32 FP32-equivalent)",
             "conv_ms_per_step": conv_ms_avg, "algorithmic_gflop_per_step": work["conv_flops"] / 1e9,
             "hbm_frac_at_min_bytes": (work["conv_bytes"] / (conv_ms_avg / 1e3) / 1e9) / peaks["hbm_gbs"],
-            "traffic": None,
+            # DRAM bytes (read + write) of the 53 conv launches of one bs256 step,
+            # from the one-pass ncu capture recorded in
+            # profiles/launch_list_bench_resnet50_bs256_ffn.md (not measured live).
+            "traffic": CONV_DRAM_BYTES_PER_STEP_BS256 * batch / 256,
+            "traffic_unit": "bytes per step (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+            "min_bytes": work["conv_bytes"],
         },
         "whole_net_tflops": work["total_flops"] / (ms_per_step / 1e3) / 1e12,
     }
