@@ -728,6 +728,49 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
           mbar_wait(&bars->residual_full[h % kSlots], (h / kSlots) & 1, &never, scratch, 39);
         }
       }
+    } else if (CTB_TM_A_TMA) {
+      // 1x1 variant (even H and W): only misaligned output / residual pointers
+      // come here. Plain loads and stores, kept small so the variant's common
+      // path does not pay for this one in registers.
+      for (int local = 0; local < my_tiles; ++local) {
+        const int buf = local & 1;
+        const long long tile = tile_index(local);
+        const int co0 = static_cast<int>(tile % co_tiles) * BN;
+        const long long pixel = tile_p0(tile / co_tiles) + quarter * 32 + lane;
+        const bool valid = quarter * 32 + lane < tile_rows(tile / co_tiles);
+        long long base = 0;
+        if (valid) {
+          const long long img = pixel / pixels_per_image;
+          base = img * p.k * pixels_per_image + (pixel - img * pixels_per_image);
+        }
+        load_params(co0);
+        const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
+        if (epilogue_any(!ready)) break;
+        tc_fence_after_sync();
+        const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll
+        for (int ci = 0; ci < kChunks; ++ci) {
+          const int ch0 = co0 + 32 * ci;
+          uint32_t v[32];
+          tmem_load_32x32(taddr + 32 * ci, v);
+          const int rows = min(32, p.k - ch0);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(v[j]);
+            if (kEpilogue != kPlain) {
+              x = (x - __shfl_sync(0xffffffffu, pm[ci], j)) * __shfl_sync(0xffffffffu, pa[ci], j) +
+                  __shfl_sync(0xffffffffu, pb[ci], j);
+            }
+            const long long at = base + static_cast<long long>(ch0 + j) * pixels_per_image;
+            if (kEpilogue == kBatchNormAddRelu && valid && j < rows) x += __ldg(residual + at);
+            if (kEpilogue == kBatchNormRelu || kEpilogue == kBatchNormAddRelu) x = fmaxf(x, 0.0f);
+            if (valid && j < rows) out[at] = x;
+          }
+        }
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
+      }
     } else {
       // Register path (pixels per image not a multiple of 4): residual
       // copied with 4-byte cp.async into the staging slots one tile ahead
