@@ -62,9 +62,19 @@ constexpr int kBK = 32;   // k per block (128 bytes of FP32)
 #define CTB_TM_GATHER_GROUPS 2
 #endif
 constexpr int kGatherGroups = CTB_TM_GATHER_GROUPS;
-constexpr int kThreads = (6 + 4 * kGatherGroups) * 32;
+// Epilogue warps: 4 (one per TMEM lane quarter), or 8 — two sets of four
+// ("halves") taking alternate 32-channel chunks, each with its own named
+// barrier, staging slots and copy-issuing threads.
+#ifndef CTB_TM_EPI_WARPS
+#define CTB_TM_EPI_WARPS 4
+#endif
+constexpr int kEpiWarps = CTB_TM_EPI_WARPS;
+constexpr int kHalves = kEpiWarps / 4;
+static_assert(kEpiWarps == 4 || kEpiWarps == 8, "epilogue warps");
+
+constexpr int kThreads = (2 + kEpiWarps + 4 * kGatherGroups) * 32;
 constexpr int kEpilogueWarp0 = 2;
-constexpr int kGatherWarp0 = 6;
+constexpr int kGatherWarp0 = kEpilogueWarp0 + kEpiWarps;
 constexpr int kGroupThreads = 128;    // four warps, one per lane quarter
 constexpr int kBoxRows = 64;          // weight rows (output channels) per TMA box
 constexpr uint32_t kBoxBytes = kBoxRows * kBK * 4;  // 8 KB
@@ -106,24 +116,36 @@ constexpr int kChunkTable = 256;                     // 4-wide k chunks describe
 constexpr int kSlots = CTB_TM_SLOTS;
 constexpr int kLoadAhead = CTB_TM_LOAD_AHEAD;
 static_assert(kSlots <= 6 && kLoadAhead < kSlots && kSlots >= 4, "staging ring");
+// Chunk h belongs to half h % kHalves; so must chunk h + kLoadAhead and every
+// chunk that reuses slot h % kSlots.
+static_assert(kLoadAhead % kHalves == 0 && kSlots % kHalves == 0, "staging ring per half");
 constexpr uint32_t kStagingBytes = kSlots * 32 * 128 * 4;
 // Activation blocks in flight (1x1 variant). A multiple of the gather group
 // count, so each slot is only ever used by one gather group: a group
 // then waits on a slot's phases strictly in order. With an odd ring the other
 // group could reach a slot's next use while its current phase is still open,
 // and a parity wait would mistake the previous completed phase for it.
-constexpr int kARing = 4;
+#ifndef CTB_TM_A_RING
+#define CTB_TM_A_RING 4
+#endif
+constexpr int kARing = CTB_TM_A_RING;
 static_assert(kARing % kGatherGroups == 0, "activation ring slots must belong to one gather group");
+// The register-path epilogue (H*W not a multiple of 4) assumes one half.
+static_assert(kEpiWarps == 4 || CTB_TM_A_TMA, "8 epilogue warps need the 1x1 variant's fallback");
 constexpr uint32_t kARingBytes = CTB_TM_A_TMA ? kARing * 32 * 128 * 4 : 0;
 
 template <int BN>
 struct Tile {
+  // Weight stages in shared memory (pack option) and activation stages in
+  // TMEM (all the columns the two accumulators leave: 4 for BN = 128, 6 for
+  // BN = 64) are separate rings with separate "empty" barriers.
   static constexpr int kStages = BN == 64 ? CTB_TM_STAGES_N64 : CTB_TM_STAGES_N128;
   static_assert(kStages <= kMaxStages, "stage count");
   static constexpr uint32_t kPlaneBytes = BN * kBK * 4;  // one of hi / lo
   static constexpr uint32_t kStageBytes = 2 * kPlaneBytes;
   static constexpr uint32_t kAColumn0 = 2 * BN;          // first activation stage column
-  static_assert(kAColumn0 + kStages * 2 * kBK <= kTmemCols, "TMEM budget");
+  static constexpr int kAStages = (kTmemCols - kAColumn0) / (2 * kBK);
+  static_assert(kAStages <= kMaxStages && kAStages % 2 == 0, "activation stages (one gather group each)");
   static_assert(kStages * kStageBytes <= kStageRegionBytes, "shared memory budget");
 };
 
@@ -136,7 +158,8 @@ struct ConvShape {
 struct __align__(8) Barriers {
   uint64_t full_a[kMaxStages];
   uint64_t full_b[kMaxStages];
-  uint64_t empty[kMaxStages];
+  uint64_t empty_a[kMaxStages];  // TMEM activation stage consumed by the MMAs
+  uint64_t empty_b[kMaxStages];  // shared-memory weight stage consumed by the MMAs
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t residual_full[6];  // bulk residual loads, one per staging slot
@@ -177,19 +200,21 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
-// Named barrier 1 over the four epilogue warps (128 threads).
-__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier 1 + half over the four warps of one epilogue half.
+__device__ __forceinline__ void epilogue_bar(int half) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
+}
 
-// OR of `pred` over the four epilogue warps; all of them get the same answer.
-__device__ __forceinline__ bool epilogue_any(bool pred) {
+// OR of `pred` over the four warps of an epilogue half; all get the same answer.
+__device__ __forceinline__ bool epilogue_any(int half, bool pred) {
   int r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.b32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 128, p;\n\t"
+      "bar.red.or.pred q, %2, 128, p;\n\t"
       "selp.b32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"(static_cast<int>(pred))
+      : "r"(static_cast<int>(pred)), "r"(1 + half)
       : "memory");
   return r != 0;
 }
@@ -292,6 +317,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
                                         const ConvShape& p, float epsilon, void* scratch) {
   using T = Tile<BN>;
   constexpr int kStages = T::kStages;
+  constexpr int kAStages = T::kAStages;
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kStageRegionBytes);
   int* chunk_table = reinterpret_cast<int*>(smem + kStageRegionBytes + kBarrierBytes);
   float* staging = reinterpret_cast<float*>(smem + kStageRegionBytes + kBarrierBytes + kChunkTable * 4);
@@ -345,15 +371,18 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->full_a[s], kGroupThreads);
       mbar_init(&bars->full_b[s], 1);
-      mbar_init(&bars->empty[s], 1);
+      mbar_init(&bars->empty_b[s], 1);
+    }
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&bars->full_a[s], kGroupThreads);
+      mbar_init(&bars->empty_a[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->tmem_full[b], 1);
-      mbar_init(&bars->tmem_empty[b], 4);
+      mbar_init(&bars->tmem_empty[b], kEpiWarps);
     }
-    for (int b = 0; b < kSlots; ++b) mbar_init(&bars->residual_full[b], 32);  // 8 issuing lanes x 4 warps
+    for (int b = 0; b < kSlots; ++b) mbar_init(&bars->residual_full[b], 32);  // 8 issuing lanes x 4 warps of a half
     for (int b = 0; b < kARing; ++b) {
       mbar_init(&bars->a_full[b], 1);
       mbar_init(&bars->a_empty[b], kGroupThreads);
@@ -415,9 +444,9 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         }
         mbar_arrive(&bars->a_empty[sa]);
       }
-      const int s = item % kStages;
-      const int use = item / kStages;
-      if (use > 0 && !mbar_wait(&bars->empty[s], (use - 1) & 1, abort, scratch, 30)) return false;
+      const int s = item % kAStages;
+      const int use = item / kAStages;
+      if (use > 0 && !mbar_wait(&bars->empty_a[s], (use - 1) & 1, abort, scratch, 30)) return false;
       tc_fence_after_sync();
       const uint32_t a_col = tmem + lane_bits + T::kAColumn0 + s * 2 * kBK;
       uint32_t hi[kBK];
@@ -460,7 +489,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       for (int kb = 0; kb < k_blocks; ++kb, ++g) {
         const int s = g % kStages;
         const int use = g / kStages;
-        if (use > 0 && !mbar_wait(&bars->empty[s], (use - 1) & 1, abort, scratch, 31)) {
+        if (use > 0 && !mbar_wait(&bars->empty_b[s], (use - 1) & 1, abort, scratch, 31)) {
           stop = true;
           break;
         }
@@ -514,17 +543,17 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       tc_fence_after_sync();
       const uint32_t acc = tmem + buf * BN;
       for (int kb = 0; kb < k_blocks; ++kb, ++g) {
-        const int s = g % kStages;
-        const uint32_t parity = (g / kStages) & 1;
-        if (!mbar_wait(&bars->full_b[s], parity, abort, scratch, 34) ||
-            !mbar_wait(&bars->full_a[s], parity, abort, scratch, 35)) {
+        const int s = g % kStages;   // weight stage
+        const int sa = g % kAStages;  // activation stage
+        if (!mbar_wait(&bars->full_b[s], (g / kStages) & 1, abort, scratch, 34) ||
+            !mbar_wait(&bars->full_a[sa], (g / kAStages) & 1, abort, scratch, 35)) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
         const uint64_t bhi = smem_desc_kmajor_sw128(b_hi(s));
         const uint64_t blo = smem_desc_kmajor_sw128(b_lo(s));
-        const uint32_t ahi = tmem + T::kAColumn0 + s * 2 * kBK;
+        const uint32_t ahi = tmem + T::kAColumn0 + sa * 2 * kBK;
         const uint32_t alo = ahi + kBK;
 #pragma unroll
         for (int kk = 0; kk < kBK / 8; ++kk) {
@@ -534,7 +563,8 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
           umma_tf32_ts(acc, ahi + 8 * kk, blo + dk, idesc, 1);
           umma_tf32_ts(acc, alo + 8 * kk, bhi + dk, idesc, 1);
         }
-        umma_commit(&bars->empty[s]);
+        umma_commit(&bars->empty_b[s]);
+        umma_commit(&bars->empty_a[sa]);
         *reinterpret_cast<volatile int*>(&bars->consumed) = g + 1;
       }
       if (ok) umma_commit(&bars->tmem_full[buf]);
@@ -544,10 +574,11 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       volatile int never = 0;
       mbar_wait(&bars->drain, 0, &never, scratch, 36);
     }
-  } else if (warp >= kEpilogueWarp0 && warp < kEpilogueWarp0 + 4) {
+  } else if (warp >= kEpilogueWarp0 && warp < kEpilogueWarp0 + kEpiWarps) {
     // ---- epilogue: lane = output pixel, 32 channels per TMEM load ----
-    const int quarter = warp & 3;          // TMEM lanes this warp may access
-    const int ew = warp - kEpilogueWarp0;  // 0..3: which channel rows this warp copies
+    const int quarter = warp & 3;                 // TMEM lanes this warp may access
+    const int ew = (warp - kEpilogueWarp0) % 4;   // 0..3: which channel rows this warp copies
+    const int half = (warp - kEpilogueWarp0) / 4;  // chunks ci with ci % kHalves == half
     constexpr int kChunks = BN / 32;
     // Folded BatchNorm terms of channel co0 + 32 i + lane, kept in registers
     // and broadcast with shuffles; reloaded only when the channel tile changes.
@@ -658,7 +689,9 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         }
       };
 #pragma unroll
-      for (int h = 0; h < kLoadAhead; ++h) load_residual(h);
+      for (int h = 0; h < kLoadAhead; ++h) {
+        if (h % kHalves == half) load_residual(h);
+      }
       int local = 0;
       for (; local < my_tiles; ++local) {
         const int buf = local & 1;
@@ -667,12 +700,13 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         const TileSpan tile_span = span_of(tile);
         load_params(co0);
         const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
-        // The four epilogue warps leave together (they share named barriers).
-        if (epilogue_any(!ready)) break;
+        // The four warps of a half leave together (they share named barriers).
+        if (epilogue_any(half, !ready)) break;
         tc_fence_after_sync();
         const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll
         for (int ci = 0; ci < kChunks; ++ci) {
+          if (ci % kHalves != half) continue;
           const int h = local * kChunks + ci;
           const int slot_id = h % kSlots;
           float* slot = staging + slot_id * 32 * kBM;
@@ -688,7 +722,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
 #pragma unroll
           for (int j = 0; j < 32; ++j) slot_px[j * kBM] = __uint_as_float(v[j]);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          epilogue_bar();  // the chunk is complete in shared memory
+          epilogue_bar(half);  // the chunk is complete in shared memory
           if (issuer) {
             const int ch = co0 + 32 * ci + row;
             if (tile_span.one_image) {
@@ -706,11 +740,12 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
               });
             }
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-            // Stores of chunks <= h - 2 have been read out of their slots.
-            asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kSlots - kLoadAhead) : "memory");
+            // This half's stores of chunks <= h + kLoadAhead - kSlots have been
+            // read out of their slots.
+            asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"((kSlots - kLoadAhead) / kHalves) : "memory");
           }
-          epilogue_bar();
-          load_residual(h + kLoadAhead);  // into slot (h - 2) % kSlots
+          epilogue_bar(half);
+          load_residual(h + kLoadAhead);  // into slot (h + kLoadAhead - kSlots) % kSlots
         }
         // Hand the accumulator back to the issuer.
         tc_fence_before_sync();
@@ -724,6 +759,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         const int consumed = local * kChunks;
         const int issued = min(total_chunks, consumed + kLoadAhead);
         for (int h = consumed; h < issued; ++h) {
+          if (h % kHalves != half) continue;
           volatile int never = 0;
           mbar_wait(&bars->residual_full[h % kSlots], (h / kSlots) & 1, &never, scratch, 39);
         }
@@ -745,11 +781,12 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         }
         load_params(co0);
         const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
-        if (epilogue_any(!ready)) break;
+        if (epilogue_any(half, !ready)) break;
         tc_fence_after_sync();
         const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll
         for (int ci = 0; ci < kChunks; ++ci) {
+          if (ci % kHalves != half) continue;
           const int ch0 = co0 + 32 * ci;
           uint32_t v[32];
           tmem_load_32x32(taddr + 32 * ci, v);
@@ -822,7 +859,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         }
         load_params(co0);
         const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
-        if (epilogue_any(!ready)) break;
+        if (epilogue_any(half, !ready)) break;
         tc_fence_after_sync();
         const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll
@@ -830,13 +867,13 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
           const int ch0 = co0 + 32 * ci;
           if (kEpilogue == kBatchNormAddRelu) {
             asm volatile("cp.async.wait_group %0;" ::"n"(kChunks - 1) : "memory");
-            epilogue_bar();  // every warp's part of chunk ci has landed
+            epilogue_bar(half);  // every warp's part of chunk ci has landed
           }
           uint32_t v[32];
           tmem_load_32x32(taddr + 32 * ci, v);
           finish_chunk(ci, staging + ci * 32 * kBM + quarter * 32 + lane, v);
           if (kEpilogue == kBatchNormAddRelu) {
-            epilogue_bar();  // slot ci is free: refill it for the next tile
+            epilogue_bar(half);  // slot ci is free: refill it for the next tile
             prefetch_residual(local + 1, ci);
           }
           const int rows = min(32, p.k - ch0);

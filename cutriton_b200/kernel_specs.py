@@ -121,7 +121,9 @@ def _conv_specs() -> list[KernelSpec]:
     def tm_defines(n128: int, n64: int, slots: int, ahead: int, a_tma: int) -> dict[str, str]:
         return {"CTB_TM_STAGES_N128": str(n128), "CTB_TM_STAGES_N64": str(n64), "CTB_TM_SLOTS": str(slots),
                 "CTB_TM_LOAD_AHEAD": str(ahead), "CTB_TM_A_TMA": str(a_tma), "CTB_TM_IMAGE_TILES": "0",
-                "CTB_TM_GATHER_GROUPS": "2"}
+                # One gather group with two epilogue halves (CTB_TM_EPI_WARPS=8) was
+                # measured slower for the 1x1 variant too: the gather limits it.
+                "CTB_TM_GATHER_GROUPS": "2", "CTB_TM_EPI_WARPS": "4"}
 
     # Epilogue tensor copies over the [N][K][H*W] view (optional: bound as
     # zeros when H*W*4 is not a multiple of 16; the kernel then stores from
