@@ -189,11 +189,16 @@ Status EncodeTensorMap(const Tensor& tensor, const KernelArgumentSource& s, CUte
   if (s.swizzle_bytes == 32) swizzle = CU_TENSOR_MAP_SWIZZLE_32B;
   if (s.swizzle_bytes == 64) swizzle = CU_TENSOR_MAP_SWIZZLE_64B;
   if (s.swizzle_bytes == 128) swizzle = CU_TENSOR_MAP_SWIZZLE_128B;
-  return drv::Check(drv::Get().cuTensorMapEncodeTiled(
-                        map, type, static_cast<cuuint32_t>(rank), address, dims, strides, box,
-                        element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
-                    "cuTensorMapEncodeTiled");
+  const CUresult result = drv::Get().cuTensorMapEncodeTiled(
+      map, type, static_cast<cuuint32_t>(rank), address, dims, strides, box, element_strides,
+      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (result != CUDA_SUCCESS && s.optional) {
+    // An optional map that does not fit this tensor is bound as zeros; the
+    // kernel checks the same conditions before using it.
+    std::memset(map, 0, sizeof(*map));
+    return Status::OK();
+  }
+  return drv::Check(result, "cuTensorMapEncodeTiled");
 }
 
 // Parameter storage for one launch. Pointers into it stay valid until the

@@ -106,6 +106,16 @@ constexpr uint32_t kTmemCols = 512;
 #ifndef CTB_TM_IMAGE_TILES
 #define CTB_TM_IMAGE_TILES 0
 #endif
+// 1 (the small-channel variant, e.g. the 7x7/2 ResNet stem): per pixel tile,
+// the whole input window its im2col touches — box {kWinW columns from -4,
+// kWinH rows from the tile's first input row, 4 channels, 1 image} of the
+// NCHW input — arrives with one TMA copy into one of two shared-memory
+// buffers, and the gather reads every tap from there with no bounds checks
+// (TMA zero-fills outside the image). Tiles whose window does not fit, or
+// that straddle two images, use the global-load gather.
+#ifndef CTB_TM_WINDOW
+#define CTB_TM_WINDOW 0
+#endif
 constexpr int kMaxStages = 6;
 constexpr uint32_t kStageRegionBytes =
     CTB_TM_STAGES_N128 * 32768 > CTB_TM_STAGES_N64 * 16384 ? CTB_TM_STAGES_N128 * 32768 : CTB_TM_STAGES_N64 * 16384;
@@ -133,6 +143,9 @@ static_assert(kARing % kGatherGroups == 0, "activation ring slots must belong to
 // The register-path epilogue (H*W not a multiple of 4) assumes one half.
 static_assert(kEpiWarps == 4 || CTB_TM_A_TMA, "8 epilogue warps need the 1x1 variant's fallback");
 constexpr uint32_t kARingBytes = CTB_TM_A_TMA ? kARing * 32 * 128 * 4 : 0;
+constexpr int kWinW = 232, kWinH = 11, kWinC = 4;
+constexpr uint32_t kWinBytes = kWinW * kWinH * kWinC * 4;
+static_assert(kWinBytes % 128 == 0, "window buffers keep 128-byte alignment");
 
 template <int BN>
 struct Tile {
@@ -165,6 +178,8 @@ struct __align__(8) Barriers {
   uint64_t residual_full[6];  // bulk residual loads, one per staging slot
   uint64_t a_full[kARing];    // activation ring (1x1 variant): TMA landed / no-copy arrival
   uint64_t a_empty[kARing];   // activation ring: the gather group has read the block
+  uint64_t win_full[2];       // input windows (small-channel variant)
+  uint64_t win_empty[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -310,7 +325,7 @@ __device__ __forceinline__ void gather_block(const PixelSource& px, const ConvSh
 template <int kEpilogue, int BN>
 __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_w, const TmaDescriptor* tma_out,
                                         const TmaDescriptor* tma_res, const TmaDescriptor* tma_x,
-                                        const float* __restrict__ x,
+                                        const TmaDescriptor* tma_xwin, const float* __restrict__ x,
                                         const float* __restrict__ scale, const float* __restrict__ bias,
                                         const float* __restrict__ mean, const float* __restrict__ variance,
                                         const float* __restrict__ residual, float* __restrict__ out,
@@ -322,6 +337,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
   int* chunk_table = reinterpret_cast<int*>(smem + kStageRegionBytes + kBarrierBytes);
   float* staging = reinterpret_cast<float*>(smem + kStageRegionBytes + kBarrierBytes + kChunkTable * 4);
   float* a_ring = staging + kStagingBytes / 4;
+  float* windows = a_ring + kARingBytes / 4;
   volatile int* abort = &bars->abort;
   auto b_hi = [&](int s) { return smem + s * T::kStageBytes; };
   auto b_lo = [&](int s) { return smem + s * T::kStageBytes + T::kPlaneBytes; };
@@ -387,6 +403,10 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       mbar_init(&bars->a_full[b], 1);
       mbar_init(&bars->a_empty[b], kGroupThreads);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->win_full[b], 1);
+      mbar_init(&bars->win_empty[b], kGatherGroups * kGroupThreads);
+    }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
     bars->consumed = 0;
@@ -404,6 +424,34 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
   if (use_table) {
     for (int i = threadIdx.x; i < k_blocks * (kBK / 4); i += blockDim.x) chunk_table[i] = chunk_entry(4 * i, cp, kdim, p.s);
   }
+  // Small-channel variant: the columns every tile touches, [-pad, (OW-1)*stride
+  // - pad + (S-1)*dil], must lie in the window's [-4, kWinW - 4); rows are
+  // checked per tile. The tensor map needs 16-byte aligned rows and base.
+  const bool window_shape = CTB_TM_WINDOW && use_table && cp == kWinC && k_blocks >= kGatherGroups &&
+                            p.pad_w <= 4 && (p.out_w - 1) * p.stride_w - p.pad_w + (p.s - 1) * p.dil_w < kWinW - 4 &&
+                            p.w % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  struct Window {
+    bool ok;
+    int img, ih_lo;
+  };
+  auto window_of = [&](long long tile) {
+    Window win{false, 0, 0};
+    if (!window_shape) return win;
+    const long long mt = tile / co_tiles;
+    const long long p0 = tile_p0(mt);
+    const int rows = tile_rows(mt);
+    const long long img = p0 / pixels_per_image;
+    const int hw0 = static_cast<int>(p0 - img * pixels_per_image);
+    if (hw0 + rows > pixels_per_image) return win;  // straddles two images
+    const int oh_a = hw0 / p.out_w, oh_b = (hw0 + rows - 1) / p.out_w;
+    const int ih_lo = oh_a * p.stride_h - p.pad_h;
+    const int ih_hi = oh_b * p.stride_h - p.pad_h + (p.r - 1) * p.dil_h;
+    if (ih_hi - ih_lo + 1 > kWinH) return win;
+    win.ok = true;
+    win.img = static_cast<int>(img);
+    win.ih_lo = ih_lo;
+    return win;
+  };
   if (warp == 0) tmem_alloc(&bars->tmem_base, kTmemCols);
   tc_fence_before_sync();
   __syncthreads();
@@ -417,16 +465,58 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     const uint32_t lane_bits = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const long long plane = static_cast<long long>(p.h) * p.w;
     const int items = my_tiles * k_blocks;  // this CTA's k blocks, in issue order
-    auto fetch = [&](int item, float (&v)[kBK]) {
+    // Returns false when the kernel is aborting (window wait abandoned).
+    auto fetch = [&](int item, float (&v)[kBK]) -> bool {
       const int local = item / k_blocks;
       const int kb = item - local * k_blocks;
       const long long tile = blockIdx.x + static_cast<long long>(local) * gridDim.x;
       int hw0, img;
-      if (tile_a_tma(tile, &hw0, &img)) return;  // arrives by TMA; read in publish
+      if (tile_a_tma(tile, &hw0, &img)) return true;  // arrives by TMA; read in publish
+      if (window_shape) {
+        // Every tile passes its buffer through the window barriers (a
+        // no-copy arrival when it uses the global-load gather), so each
+        // group waits for the tile's window before its first item of the
+        // tile and releases it after its last.
+        const int wb = local & 1;
+        const int first = local * k_blocks + ((group - local * k_blocks) % kGatherGroups + kGatherGroups) % kGatherGroups;
+        const int last_end = (local + 1) * k_blocks;
+        if (item == first &&
+            !mbar_wait(&bars->win_full[wb], (local >> 1) & 1, abort, scratch, 43)) {
+          return false;
+        }
+        const Window win = window_of(tile);
+        if (win.ok) {
+          const long long mt = tile / co_tiles;
+          const bool valid = row < tile_rows(mt);
+          const long long pixel = tile_p0(mt) + row;
+          const int rem = static_cast<int>(pixel - static_cast<long long>(win.img) * pixels_per_image);
+          const int oh = rem / p.out_w;
+          const int ow = rem - oh * p.out_w;
+          const int base = (oh * p.stride_h - p.pad_h - win.ih_lo) * kWinW + ow * p.stride_w - p.pad_w + 4;
+          const float* win_buf = windows + wb * (kWinBytes / 4);
+#pragma unroll
+          for (int j = 0; j < kBK / 4; ++j) {
+            const int e = chunk_table[kb * (kBK / 4) + j];
+            const int off = base + ((e >> 10) & 1023) * p.dil_h * kWinW + (e & 1023) * p.dil_w;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              v[4 * j + i] = (valid && e >= 0 && i < p.c) ? win_buf[i * kWinH * kWinW + off] : 0.0f;
+            }
+          }
+        } else {
+          const PixelSource px =
+              pixel_source(x, p, row < tile_rows(tile / co_tiles) ? tile_p0(tile / co_tiles) + row : total_pixels,
+                           total_pixels, pixels_per_image);
+          gather_block(px, p, cp, kdim, plane, kb, chunk_table, v);
+        }
+        if (item + kGatherGroups >= last_end) mbar_arrive(&bars->win_empty[wb]);  // group's last item of the tile
+        return true;
+      }
       const PixelSource px =
           pixel_source(x, p, row < tile_rows(tile / co_tiles) ? tile_p0(tile / co_tiles) + row : total_pixels,
                        total_pixels, pixels_per_image);
       gather_block(px, p, cp, kdim, plane, kb, use_table ? chunk_table : nullptr, v);
+      return true;
     };
     // Splits one block into hi / lo and writes it to the stage's TMEM columns.
     // Returns false when the kernel is aborting.
@@ -467,25 +557,39 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     // nothing waits on the prefetch early).
     float buf_a[kBK], buf_b[kBK];
     int item = group;
-    if (item < items) fetch(item, buf_a);
+    if (item < items && !fetch(item, buf_a)) item = items;
     while (item < items) {
-      if (item + kGatherGroups < items) fetch(item + kGatherGroups, buf_b);
+      if (item + kGatherGroups < items && !fetch(item + kGatherGroups, buf_b)) break;
       if (!publish(item, buf_a)) break;
       item += kGatherGroups;
       if (item >= items) break;
-      if (item + kGatherGroups < items) fetch(item + kGatherGroups, buf_a);
+      if (item + kGatherGroups < items && !fetch(item + kGatherGroups, buf_a)) break;
       if (!publish(item, buf_b)) break;
       item += kGatherGroups;
     }
   } else if (warp == 0 && lane == 0) {
     // ---- TMA producer: weight hi / lo tiles ----
+    if (window_shape) tma_prefetch(tma_xwin);
     int g = 0;
+    int windows_issued = 0;
     bool stop = false;
     for (int local = 0; local < my_tiles && !stop; ++local) {
       const long long tile = blockIdx.x + static_cast<long long>(local) * gridDim.x;
       const int co0 = static_cast<int>(tile % co_tiles) * BN;
       int a_hw0 = 0, a_img = 0;
       const bool tile_uses_a_tma = tile_a_tma(tile, &a_hw0, &a_img);
+      if (window_shape) {
+        const int wb = local & 1;
+        if (local >= 2 && !mbar_wait(&bars->win_empty[wb], ((local >> 1) - 1) & 1, abort, scratch, 44)) break;
+        const Window win = window_of(tile);
+        if (win.ok) {
+          mbar_arrive_expect_tx(&bars->win_full[wb], kWinBytes);
+          tma_load_4d(windows + wb * (kWinBytes / 4), tma_xwin, &bars->win_full[wb], -4, win.ih_lo, 0, win.img);
+        } else {
+          mbar_arrive(&bars->win_full[wb]);
+        }
+        windows_issued = local + 1;
+      }
       for (int kb = 0; kb < k_blocks; ++kb, ++g) {
         const int s = g % kStages;
         const int use = g / kStages;
@@ -520,6 +624,13 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       for (int q = *reinterpret_cast<volatile int*>(&bars->consumed); q < g; ++q) {
         volatile int never = 0;
         mbar_wait(&bars->full_b[q % kStages], (q / kStages) & 1, &never, scratch, 32);
+      }
+      if (window_shape) {
+        // At most the two newest windows can still be in flight.
+        for (int q = max(0, windows_issued - 2); q < windows_issued; ++q) {
+          volatile int never = 0;
+          mbar_wait(&bars->win_full[q & 1], (q >> 1) & 1, &never, scratch, 45);
+        }
       }
       if (CTB_TM_A_TMA) {
         // At most one activation copy per ring slot can be outstanding.
@@ -904,16 +1015,16 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
 template <int kEpilogue>
 __device__ __forceinline__ void conv_tm_dispatch(const TmaDescriptor* tma_w, const TmaDescriptor* tma_out,
                                                  const TmaDescriptor* tma_res, const TmaDescriptor* tma_x,
-                                                 const float* x, const float* scale,
+                                                 const TmaDescriptor* tma_xwin, const float* x, const float* scale,
                                                  const float* bias, const float* mean, const float* variance,
                                                  const float* residual, float* out, const ConvShape& p,
                                                  float epsilon, void* scratch) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   if (p.k <= 64) {
-    conv_tm<kEpilogue, 64>(smem, tma_w, tma_out, tma_res, tma_x, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
+    conv_tm<kEpilogue, 64>(smem, tma_w, tma_out, tma_res, tma_x, tma_xwin, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
   } else {
-    conv_tm<kEpilogue, 128>(smem, tma_w, tma_out, tma_res, tma_x, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
+    conv_tm<kEpilogue, 128>(smem, tma_w, tma_out, tma_res, tma_x, tma_xwin, x, scale, bias, mean, variance, residual, out, p, epsilon, scratch);
   }
 }
 
@@ -930,7 +1041,7 @@ ctb_conv_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const __grid_consta
                 const __grid_constant__ TmaDescriptor tma_x, const float* x, float* output, CTB_CONV_DIMS,
                 CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kPlain>(&tma_w, &tma_out, nullptr, &tma_x, x, nullptr, nullptr, nullptr, nullptr, nullptr, output, CTB_CONV_SHAPE, 0.0f,
+  conv_tm_dispatch<kPlain>(&tma_w, &tma_out, nullptr, &tma_x, nullptr, x, nullptr, nullptr, nullptr, nullptr, nullptr, output, CTB_CONV_SHAPE, 0.0f,
                            runtime_scratch);
 }
 
@@ -939,16 +1050,17 @@ ctb_conv_bn_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const __grid_con
                    const __grid_constant__ TmaDescriptor tma_x, const float* x, const float* scale, const float* bias, const float* mean, const float* variance,
                    float* output, CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kBatchNorm>(&tma_w, &tma_out, nullptr, &tma_x, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE, epsilon,
+  conv_tm_dispatch<kBatchNorm>(&tma_w, &tma_out, nullptr, &tma_x, nullptr, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE, epsilon,
                                runtime_scratch);
 }
 
 extern "C" __global__ void __launch_bounds__(kThreads, 1)
 ctb_conv_bn_relu_f32_tm(const __grid_constant__ TmaDescriptor tma_w, const __grid_constant__ TmaDescriptor tma_out,
-                        const __grid_constant__ TmaDescriptor tma_x, const float* x, const float* scale, const float* bias, const float* mean,
+                        const __grid_constant__ TmaDescriptor tma_x, const __grid_constant__ TmaDescriptor tma_xwin,
+                        const float* x, const float* scale, const float* bias, const float* mean,
                         const float* variance, float* output, CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kBatchNormRelu>(&tma_w, &tma_out, nullptr, &tma_x, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE,
+  conv_tm_dispatch<kBatchNormRelu>(&tma_w, &tma_out, nullptr, &tma_x, &tma_xwin, x, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE,
                                    epsilon, runtime_scratch);
 }
 
@@ -960,6 +1072,6 @@ ctb_conv_bn_add_relu_f32_tm(const __grid_constant__ TmaDescriptor tma_w,
                             const float* bias, const float* mean, const float* variance, const float* residual,
                             float* output, CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
-  conv_tm_dispatch<kBatchNormAddRelu>(&tma_w, &tma_out, &tma_res, &tma_x, x, scale, bias, mean, variance, residual, output, CTB_CONV_SHAPE,
+  conv_tm_dispatch<kBatchNormAddRelu>(&tma_w, &tma_out, &tma_res, &tma_x, nullptr, x, scale, bias, mean, variance, residual, output, CTB_CONV_SHAPE,
                                       epsilon, runtime_scratch);
 }

@@ -143,24 +143,40 @@ def _conv_specs() -> list[KernelSpec]:
         {"kind": "dim_multiple_of", "source": "output", "index": 0, "axis": 2, "value": 2},
         {"kind": "dim_multiple_of", "source": "output", "index": 0, "axis": 3, "value": 2},
     )
+    # Input windows of the small-channel variant: box {232 columns, 11 rows,
+    # 4 channels, 1 image} of the NCHW input (the 7x7/2 stem's tile window).
+    tma_xwin = arg("tma_xwin", "tensormap", "tensor_map", tensor="input", index=0, box=[232, 11, 4, 1], optional=1)
+    tiny_box = {"tma_xwin": {"box": [4, 1, 1, 1]}}  # unused by the other variants
+    window_bytes = 2 * 232 * 11 * 4 * 4
     for kernel_id, op_type, symbol, arguments in tc_families:
-        maps = (tma_w64, tma_out) + ((tma_res,) if op_type.endswith("AddRelu") else ()) + (tma_x,)
+        with_window = op_type == "FusedConvBatchNormRelu"
+        maps = ((tma_w64, tma_out) + ((tma_res,) if op_type.endswith("AddRelu") else ()) + (tma_x,)
+                + ((tma_xwin,) if with_window else ()))
+        overrides = tiny_box if with_window else {}
+        variants = [
+            # Any shape: activations gathered with global loads.
+            Variant("persistent_m128n128k32_tmem_a_3xtf32", num_warps=14,
+                    shared_memory_bytes=tm_smem(3, 6, 4, 0), defines=tm_defines(3, 6, 4, 2, 0),
+                    meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, arg_overrides=overrides),
+            # 1x1 / stride 1 / no padding: activation blocks by TMA.
+            Variant("persistent_m128n128k32_tmem_a_3xtf32_1x1tma", num_warps=14,
+                    shared_memory_bytes=tm_smem(3, 5, 4, 4), defines=tm_defines(3, 5, 4, 2, 1),
+                    meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, constraints=one_by_one, default=True,
+                    arg_overrides=overrides),
+        ]
+        if with_window:
+            # C <= 4 (the stem): listed first so it leads when the 1x1 default does not apply.
+            variants.insert(0, Variant(
+                "persistent_m128n128k32_tmem_a_3xtf32_window", num_warps=14,
+                shared_memory_bytes=tm_smem(2, 4, 4, 0) + window_bytes,
+                defines={**tm_defines(2, 4, 4, 2, 0), "CTB_TM_WINDOW": "1"},
+                meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128},
+                constraints=({"kind": "dim_le", "source": "input", "index": 1, "axis": 1, "value": 4},)))
         specs.append(KernelSpec(
             kernel_id=kernel_id.replace("tcgen05", "tcgen05_tmem"), op_type=op_type, version=1,
             source="conv_tm.cu", symbol=symbol.replace("_tc", "_tm"),
             arguments=maps + arguments[1:], grid=tc_grid, layout="NCHW",
-            constraints=({"kind": "input_is_constant", "index": 1},),
-            variants=(
-                # Any shape: activations gathered with global loads.
-                Variant("persistent_m128n128k32_tmem_a_3xtf32", num_warps=14,
-                        shared_memory_bytes=tm_smem(3, 6, 4, 0), defines=tm_defines(3, 6, 4, 2, 0),
-                        meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}),
-                # 1x1 / stride 1 / no padding: activation blocks by TMA.
-                Variant("persistent_m128n128k32_tmem_a_3xtf32_1x1tma", num_warps=14,
-                        shared_memory_bytes=tm_smem(3, 5, 4, 4), defines=tm_defines(3, 5, 4, 2, 1),
-                        meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, constraints=one_by_one, default=True),
-            ),
-        ))
+            constraints=({"kind": "input_is_constant", "index": 1},), variants=tuple(variants)))
     for kernel_id, op_type, symbol, arguments in tc_families:
         stages = 3
         smem = stages * 65536 + 4 * 32 * 33 * 4 + 1024 + 256

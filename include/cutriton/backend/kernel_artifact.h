@@ -56,8 +56,9 @@ struct KernelArgumentSource {
   // (0, 32, 64 or 128). merge_inner > 1 folds that many innermost tensor
   // dimensions into one (e.g. H, W -> H*W); the box then lists one extent
   // for the folded dimension. An optional map whose strides or base are not
-  // 16-byte aligned is bound as all zeros instead of failing the launch (the
-  // kernel must not use it then).
+  // 16-byte aligned, or that the driver cannot encode for this tensor, is
+  // bound as all zeros instead of failing the launch (the kernel must not use
+  // it then).
   bool map_output{false};
   std::vector<int64_t> box;
   int swizzle_bytes{0};

@@ -65,6 +65,7 @@ CONV_CASES = [
     (1, 37, 9, 11, 19, 3, 1, 1),      # ragged everything
     (8, 64, 56, 56, 256, 1, 1, 0),    # > 2 persistent tiles per CTA (128-channel tiles)
     (8, 64, 56, 56, 64, 1, 1, 0),     # > 1 persistent tile per CTA (64-channel tiles)
+    (2, 3, 224, 224, 64, 7, 2, 3),    # the ResNet stem: TMA input windows (small-channel variant)
 ]
 
 
