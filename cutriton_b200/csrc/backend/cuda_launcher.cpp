@@ -149,9 +149,14 @@ Status EncodeTensorMap(const Tensor& tensor, const KernelArgumentSource& s, CUte
   const TensorDesc& desc = tensor.desc();
   const std::size_t tensor_rank = desc.shape.size();
   const std::size_t merge = static_cast<std::size_t>(s.merge_inner);
-  if (merge > tensor_rank) return Status::ShapeError("tensor_map merge_inner exceeds the tensor rank");
+  if (merge > tensor_rank || tensor_rank - merge + 1 != s.box.size()) {
+    if (s.optional) {  // a map that does not fit this tensor's rank is bound as zeros
+      std::memset(map, 0, sizeof(*map));
+      return Status::OK();
+    }
+    return Status::ShapeError("tensor_map box rank differs from the tensor rank");
+  }
   const std::size_t rank = tensor_rank - merge + 1;
-  if (rank != s.box.size()) return Status::ShapeError("tensor_map box rank differs from the tensor rank");
   CUtensorMapDataType type;
   switch (desc.dtype) {
     case DataType::kFloat32: type = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; break;

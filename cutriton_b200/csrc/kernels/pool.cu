@@ -57,3 +57,47 @@ ctb_global_average_pool_f32(const float* __restrict__ x, float* __restrict__ out
   sum = ctb::warp_sum(sum);
   if (lane == 0) out[plane] = sum / static_cast<float>(spatial);
 }
+
+// MaxPool 3x3 / stride 2 / pad 1 with W % 4 == 0 and W <= 128 (the ResNet-50
+// stem pool): one warp per output row. Lane L loads columns 4L..4L+3 of the
+// three input rows as float4 (one 16-byte, fully coalesced access per row)
+// and produces outputs 2L (columns 4L-1..4L+1; column 4L-1 is lane L-1's .w,
+// passed by a shuffle) and 2L+1 (columns 4L+1..4L+3). Same fmaxf over the
+// same taps as ctb_max_pool_f32, so the results are identical.
+extern "C" __global__ void __launch_bounds__(256)
+ctb_max_pool_3x3s2_f32(const float* __restrict__ x, float* __restrict__ out, int n, int c, int h, int w,
+                       int out_h, int out_w, CTB_RESERVED_PARAMS) {
+  CTB_UNUSED_RESERVED();
+  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= static_cast<long long>(n) * c * out_h) return;  // warp-uniform
+  const long long plane = row / out_h;
+  const int oh = static_cast<int>(row - plane * out_h);
+  const float* src = x + plane * h * w;
+  const int quads = w / 4;
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  float o0 = -CUDART_INF_F, o1 = -CUDART_INF_F;
+#pragma unroll
+  for (int dr = -1; dr <= 1; ++dr) {
+    const int ih = 2 * oh + dr;
+    const bool row_ok = ih >= 0 && ih < h;
+    float4 v = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F);
+    if (row_ok && lane < quads) {
+      const float* p = src + static_cast<long long>(ih) * w + 4 * lane;
+      if (vec) {
+        v = __ldg(reinterpret_cast<const float4*>(p));
+      } else {
+        v = make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
+      }
+    }
+    float left = __shfl_up_sync(0xffffffffu, v.w, 1);
+    if (lane == 0) left = -CUDART_INF_F;  // column -1: padding
+    o0 = fmaxf(o0, fmaxf(fmaxf(left, v.x), v.y));
+    o1 = fmaxf(o1, fmaxf(fmaxf(v.y, v.z), v.w));
+  }
+  if (lane < quads) {
+    float* dst = out + row * out_w + 2 * lane;
+    dst[0] = o0;
+    dst[1] = o1;
+  }
+}

@@ -265,7 +265,28 @@ def _pool_specs() -> list[KernelSpec]:
             kernel_id="max_pool.fp32.nchw", op_type="MaxPool", version=1, source="pool.cu",
             symbol="ctb_max_pool_f32", arguments=pool_arguments, layout="NCHW",
             grid=(ceil_div(out_numel(), meta("BLOCK")),),
-            variants=(Variant("thread_per_output", num_warps=8, meta={"BLOCK": 256}, default=True),),
+            variants=(Variant("thread_per_output", num_warps=8, meta={"BLOCK": 256}, default=False),),
+        ),
+        # 3x3/2 pad 1 with W % 4 == 0 and W <= 128: warp per output row, float4 rows.
+        KernelSpec(
+            kernel_id="max_pool_3x3s2.fp32.nchw", op_type="MaxPool", version=1, source="pool.cu",
+            symbol="ctb_max_pool_3x3s2_f32",
+            arguments=(arg("x", "*fp32", "input", index=0), arg("output", "*fp32", "output", index=0),
+                       arg("n", "i32", "input_dim", index=0, axis=0), arg("c", "i32", "input_dim", index=0, axis=1),
+                       arg("h", "i32", "input_dim", index=0, axis=2), arg("w", "i32", "input_dim", index=0, axis=3),
+                       arg("out_h", "i32", "output_dim", index=0, axis=2),
+                       arg("out_w", "i32", "output_dim", index=0, axis=3)) + RESERVED,
+            layout="NCHW", grid=(ceil_div(mul(out_dim(0), mul(out_dim(1), out_dim(2))), meta("ROWS")),),
+            constraints=(
+                {"kind": "attribute_list_eq", "name": "kernel_shape", "value": [3, 3], "default": [0, 0]},
+                {"kind": "attribute_list_eq", "name": "strides", "value": [2, 2], "default": [1, 1]},
+                {"kind": "attribute_list_eq", "name": "pads", "value": [1, 1, 1, 1], "default": [0, 0, 0, 0]},
+                {"kind": "attribute_list_eq", "name": "dilations", "value": [1, 1], "default": [1, 1]},
+                {"kind": "dim_multiple_of", "source": "input", "index": 0, "axis": 3, "value": 4},
+                {"kind": "dim_le", "source": "input", "index": 0, "axis": 3, "value": 128},
+                {"kind": "dim_multiple_of", "source": "input", "index": 0, "axis": 2, "value": 2},
+            ),
+            variants=(Variant("warp_per_row_vec4", num_warps=8, meta={"ROWS": 8}, default=True),),
         ),
         KernelSpec(
             kernel_id="global_average_pool.fp32.nchw", op_type="GlobalAveragePool", version=1, source="pool.cu",
@@ -355,11 +376,51 @@ def _gemm_specs() -> list[KernelSpec]:
                    symbol="ctb_gemm_gelu_f16_tc", arguments=tc_args(128), grid=grid, dtype="float16",
                    constraints=tc_constraints, variants=tc_variants()),
     ]
-    return tc + [
+    # FP32 Gemm on the tensor cores: the TMEM conv kernel (3xTF32) as a 1x1
+    # convolution over M "pixels" with H = W = 1; B [K, N] prepacked to the
+    # K-major hi / lo planes [2][N][K] ("gemm_w_tf32x2_nk"). Its tensor maps
+    # over the output / input do not fit a rank-2 tensor and are bound as
+    # zeros, which selects the kernel's register-path epilogue.
+    one = {"default": 1}
+    zero = {"default": 0}
+    fp32_tm_args = (
+        arg("tma_w", "tensormap", "tensor_map", tensor="input", index=1, box=[32, 64, 1], swizzle=128,
+            prepack="gemm_w_tf32x2_nk"),
+        arg("tma_out", "tensormap", "tensor_map", tensor="output", index=0, box=[128, 32, 1], merge_inner=2,
+            optional=1),
+        arg("tma_x", "tensormap", "tensor_map", tensor="input", index=0, box=[128, 32, 1], merge_inner=2,
+            optional=1),
+        arg("x", "*fp32", "input", index=0),
+        arg("output", "*fp32", "output", index=0),
+        arg("n", "i32", "input_dim", index=0, axis=0),
+        arg("c", "i32", "input_dim", index=0, axis=1),
+        arg("h", "i32", "literal_i32", **one), arg("w", "i32", "literal_i32", **one),
+        arg("k", "i32", "output_dim", index=0, axis=1),
+        arg("r", "i32", "literal_i32", **one), arg("s", "i32", "literal_i32", **one),
+        arg("out_h", "i32", "literal_i32", **one), arg("out_w", "i32", "literal_i32", **one),
+        arg("stride_h", "i32", "literal_i32", **one), arg("stride_w", "i32", "literal_i32", **one),
+        arg("pad_h", "i32", "literal_i32", **zero), arg("pad_w", "i32", "literal_i32", **zero),
+        arg("dilation_h", "i32", "literal_i32", **one), arg("dilation_w", "i32", "literal_i32", **one),
+    ) + RESERVED
+    fp32_tm_grid = ({"kind": "min", "args": [mul(ceil_div(out_dim(0), literal(128)), ceil_div(out_dim(1), literal(128))),
+                                             {"kind": "sm_count"}]},)
+    fp32_tm_smem = 3 * 32768 + 512 + 1024 + 4 * 16384 + 1024
+    fp32_tm = KernelSpec(
+        kernel_id="gemm.fp32.tcgen05_tmem", op_type="Gemm", version=1, source="conv_tm.cu", symbol="ctb_conv_f32_tm",
+        arguments=fp32_tm_args, grid=fp32_tm_grid,
+        constraints=GEMM_CONSTRAINTS + ({"kind": "input_is_constant", "index": 1},
+                                        {"kind": "dim_multiple_of", "source": "input", "index": 0, "axis": 1,
+                                         "value": 4}),
+        variants=(Variant("persistent_m128n128k32_tmem_a_3xtf32", num_warps=14, shared_memory_bytes=fp32_tm_smem,
+                          defines={"CTB_TM_STAGES_N128": "3", "CTB_TM_STAGES_N64": "6", "CTB_TM_SLOTS": "4",
+                                   "CTB_TM_LOAD_AHEAD": "2", "CTB_TM_A_TMA": "0", "CTB_TM_IMAGE_TILES": "0",
+                                   "CTB_TM_GATHER_GROUPS": "2", "CTB_TM_EPI_WARPS": "4"}, default=True),),
+    )
+    return tc + [fp32_tm] + [
         KernelSpec(
             kernel_id="gemm.fp32", op_type="Gemm", version=1, source="conv_simt.cu", symbol="ctb_gemm_f32_simt",
             arguments=gemm_args("*fp32"), grid=grid, constraints=GEMM_CONSTRAINTS,
-            variants=(Variant("simt_m64n64", num_warps=8, meta=SIMT_TILE, default=True),),
+            variants=(Variant("simt_m64n64", num_warps=8, meta=SIMT_TILE, default=False),),
         ),
         KernelSpec(
             kernel_id="gemm.fp16.wmma", op_type="Gemm", version=1, source="gemm_f16_wmma.cu",

@@ -100,7 +100,7 @@ def test_conv_family_all_candidates(cuda, case, op):
         assert_close(out["y"], expected, atol=tol, rtol=tol, what=f"{op} {case} {cand}")
 
 
-@pytest.mark.parametrize("shape", [(2, 64, 112, 112), (3, 5, 7, 9), (1, 1, 1, 1)])
+@pytest.mark.parametrize("shape", [(2, 64, 112, 112), (3, 5, 7, 9), (1, 1, 1, 1), (2, 3, 9, 128)])
 def test_max_pool_bitexact(cuda, shape):
     x = randn(*shape)
     x.flat[::7] = -np.inf
@@ -110,8 +110,10 @@ def test_max_pool_bitexact(cuda, shape):
                    dilations=[1, 1])
     model.add_output("y")
     expected = oracle.max_pool(x)
-    out, _ = run_graph(model, {"x": x}, {"y": (expected.shape, np.float32)})
-    assert_bitexact(out["y"], expected, "MaxPool")
+    engine = ct.build_engine(model)
+    for index, cand in enumerate(engine.ops()[0]["candidates"]):
+        out, _ = run_graph(model, {"x": x}, {"y": (expected.shape, np.float32)}, candidate=(0, index))
+        assert_bitexact(out["y"], expected, f"MaxPool {cand}")
 
 
 @pytest.mark.parametrize("shape", [(4, 2048, 7, 7), (3, 17, 5, 3)])
