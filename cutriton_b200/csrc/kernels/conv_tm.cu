@@ -116,6 +116,15 @@ constexpr uint32_t kTmemCols = 512;
 #ifndef CTB_TM_WINDOW
 #define CTB_TM_WINDOW 0
 #endif
+// 1: 64-channel tiles issue 2 instead of 3 UMMAs per 8 k: A_hi . [B_hi; B_lo]
+// (N = 128 over the stacked hi / lo weight planes, which sit contiguously in
+// shared memory) into one accumulator and A_lo . B_hi (N = 64) into another;
+// the epilogue adds the three 64-column products. Fewer, wider instructions
+// for a pipe bound by per-instruction cost; TMEM then holds two activation
+// stages (2 x 192 accumulator columns + 2 x 64).
+#ifndef CTB_TM_SPLIT_N
+#define CTB_TM_SPLIT_N 0
+#endif
 constexpr int kMaxStages = 6;
 constexpr uint32_t kStageRegionBytes =
     CTB_TM_STAGES_N128 * 32768 > CTB_TM_STAGES_N64 * 16384 ? CTB_TM_STAGES_N128 * 32768 : CTB_TM_STAGES_N64 * 16384;
@@ -156,7 +165,9 @@ struct Tile {
   static_assert(kStages <= kMaxStages, "stage count");
   static constexpr uint32_t kPlaneBytes = BN * kBK * 4;  // one of hi / lo
   static constexpr uint32_t kStageBytes = 2 * kPlaneBytes;
-  static constexpr uint32_t kAColumn0 = 2 * BN;          // first activation stage column
+  static constexpr bool kSplitN = CTB_TM_SPLIT_N && BN == 64;
+  static constexpr uint32_t kAccCols = kSplitN ? 3 * BN : BN;  // one accumulator buffer
+  static constexpr uint32_t kAColumn0 = 2 * kAccCols;  // first activation stage column
   static constexpr int kAStages = (kTmemCols - kAColumn0) / (2 * kBK);
   static_assert(kAStages <= kMaxStages && kAStages % 2 == 0, "activation stages (one gather group each)");
   static_assert(kStages * kStageBytes <= kStageRegionBytes, "shared memory budget");
@@ -652,7 +663,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         break;
       }
       tc_fence_after_sync();
-      const uint32_t acc = tmem + buf * BN;
+      const uint32_t acc = tmem + buf * T::kAccCols;
       for (int kb = 0; kb < k_blocks; ++kb, ++g) {
         const int s = g % kStages;   // weight stage
         const int sa = g % kAStages;  // activation stage
@@ -670,9 +681,16 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         for (int kk = 0; kk < kBK / 8; ++kk) {
           // 8 TF32 values along k: 8 TMEM columns of A, +32 bytes inside B's rows.
           const uint64_t dk = 2 * kk;
-          umma_tf32_ts(acc, ahi + 8 * kk, bhi + dk, idesc, (kb | kk) != 0);
-          umma_tf32_ts(acc, ahi + 8 * kk, blo + dk, idesc, 1);
-          umma_tf32_ts(acc, alo + 8 * kk, bhi + dk, idesc, 1);
+          if (T::kSplitN) {
+            // [B_hi; B_lo] as one 128-row operand: b_lo(s) follows b_hi(s).
+            constexpr uint32_t idesc_wide = instr_desc(kFormatTF32, kBM, 2 * BN);
+            umma_tf32_ts(acc, ahi + 8 * kk, bhi + dk, idesc_wide, (kb | kk) != 0);
+            umma_tf32_ts(acc + 2 * BN, alo + 8 * kk, bhi + dk, idesc, (kb | kk) != 0);
+          } else {
+            umma_tf32_ts(acc, ahi + 8 * kk, bhi + dk, idesc, (kb | kk) != 0);
+            umma_tf32_ts(acc, ahi + 8 * kk, blo + dk, idesc, 1);
+            umma_tf32_ts(acc, alo + 8 * kk, bhi + dk, idesc, 1);
+          }
         }
         umma_commit(&bars->empty_b[s]);
         umma_commit(&bars->empty_a[sa]);
@@ -727,6 +745,19 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       }
     };
     auto tile_index = [&](int local) { return blockIdx.x + static_cast<long long>(local) * gridDim.x; };
+    // Accumulator chunk ci (32 channels) of this warp's 32 rows.
+    auto load_acc = [&](uint32_t taddr, int ci, uint32_t (&v)[32]) {
+      tmem_load_32x32(taddr + 32 * ci, v);
+      if (T::kSplitN) {
+        uint32_t t[32];
+        tmem_load_32x32(taddr + BN + 32 * ci, t);  // A_hi . B_lo
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(t[j]));
+        tmem_load_32x32(taddr + 2 * BN + 32 * ci, t);  // A_lo . B_hi
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(t[j]));
+      }
+    };
 
     if (bulk_epilogue) {
       // Bulk path: every 4-pixel group lies inside one image, so each channel
@@ -814,7 +845,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         // The four warps of a half leave together (they share named barriers).
         if (epilogue_any(half, !ready)) break;
         tc_fence_after_sync();
-        const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t taddr = tmem + buf * T::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll
         for (int ci = 0; ci < kChunks; ++ci) {
           if (ci % kHalves != half) continue;
@@ -827,7 +858,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
             mbar_wait(&bars->residual_full[slot_id], (h / kSlots) & 1, abort, scratch, 38);
           }
           uint32_t v[32];
-          tmem_load_32x32(taddr + 32 * ci, v);
+          load_acc(taddr, ci, v);
           float* slot_px = slot + quarter * 32 + lane;
           finish_chunk(ci, slot_px, v);
 #pragma unroll
@@ -894,13 +925,13 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
         if (epilogue_any(half, !ready)) break;
         tc_fence_after_sync();
-        const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t taddr = tmem + buf * T::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll
         for (int ci = 0; ci < kChunks; ++ci) {
           if (ci % kHalves != half) continue;
           const int ch0 = co0 + 32 * ci;
           uint32_t v[32];
-          tmem_load_32x32(taddr + 32 * ci, v);
+          load_acc(taddr, ci, v);
           const int rows = min(32, p.k - ch0);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -972,7 +1003,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
         if (epilogue_any(half, !ready)) break;
         tc_fence_after_sync();
-        const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t taddr = tmem + buf * T::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll
         for (int ci = 0; ci < kChunks; ++ci) {
           const int ch0 = co0 + 32 * ci;
@@ -981,7 +1012,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
             epilogue_bar(half);  // every warp's part of chunk ci has landed
           }
           uint32_t v[32];
-          tmem_load_32x32(taddr + 32 * ci, v);
+          load_acc(taddr, ci, v);
           finish_chunk(ci, staging + ci * 32 * kBM + quarter * 32 + lane, v);
           if (kEpilogue == kBatchNormAddRelu) {
             epilogue_bar(half);  // slot ci is free: refill it for the next tile

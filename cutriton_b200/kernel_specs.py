@@ -123,7 +123,7 @@ def _conv_specs() -> list[KernelSpec]:
                 "CTB_TM_LOAD_AHEAD": str(ahead), "CTB_TM_A_TMA": str(a_tma), "CTB_TM_IMAGE_TILES": "0",
                 # One gather group with two epilogue halves (CTB_TM_EPI_WARPS=8) was
                 # measured slower for the 1x1 variant too: the gather limits it.
-                "CTB_TM_GATHER_GROUPS": "2", "CTB_TM_EPI_WARPS": "4"}
+                "CTB_TM_GATHER_GROUPS": "2", "CTB_TM_EPI_WARPS": "4", "CTB_TM_SPLIT_N": "1"}
 
     # Epilogue tensor copies over the [N][K][H*W] view (optional: bound as
     # zeros when H*W*4 is not a multiple of 16; the kernel then stores from
@@ -414,7 +414,7 @@ def _gemm_specs() -> list[KernelSpec]:
         variants=(Variant("persistent_m128n128k32_tmem_a_3xtf32", num_warps=14, shared_memory_bytes=fp32_tm_smem,
                           defines={"CTB_TM_STAGES_N128": "3", "CTB_TM_STAGES_N64": "6", "CTB_TM_SLOTS": "4",
                                    "CTB_TM_LOAD_AHEAD": "2", "CTB_TM_A_TMA": "0", "CTB_TM_IMAGE_TILES": "0",
-                                   "CTB_TM_GATHER_GROUPS": "2", "CTB_TM_EPI_WARPS": "4"}, default=True),),
+                                   "CTB_TM_GATHER_GROUPS": "2", "CTB_TM_EPI_WARPS": "4", "CTB_TM_SPLIT_N": "1"}, default=True),),
     )
     return tc + [fp32_tm] + [
         KernelSpec(
