@@ -118,12 +118,18 @@ constexpr uint32_t kTmemCols = 512;
 #endif
 // 1: 64-channel tiles issue 2 instead of 3 UMMAs per 8 k: A_hi . [B_hi; B_lo]
 // (N = 128 over the stacked hi / lo weight planes, which sit contiguously in
-// shared memory) into one accumulator and A_lo . B_hi (N = 64) into another;
-// the epilogue adds the three 64-column products. Fewer, wider instructions
-// for a pipe bound by per-instruction cost; TMEM then holds two activation
-// stages (2 x 192 accumulator columns + 2 x 64).
+// shared memory) into a 128-column accumulator, then A_lo . B_hi (N = 64)
+// accumulated into its first 64 columns (the tensor pipe runs them in
+// order); the epilogue adds the two halves. Fewer, wider instructions for a
+// pipe bound by per-instruction cost, in the same TMEM as the 3-UMMA form.
 #ifndef CTB_TM_SPLIT_N
 #define CTB_TM_SPLIT_N 0
+#endif
+// 1: the same for 128-channel tiles (A_hi . [B_hi; B_lo] as one N = 256
+// UMMA); the 256-column accumulator then fits once, so the epilogue of a tile
+// no longer overlaps the next tile's MMAs.
+#ifndef CTB_TM_SPLIT_N128
+#define CTB_TM_SPLIT_N128 0
 #endif
 constexpr int kMaxStages = 6;
 constexpr uint32_t kStageRegionBytes =
@@ -165,9 +171,10 @@ struct Tile {
   static_assert(kStages <= kMaxStages, "stage count");
   static constexpr uint32_t kPlaneBytes = BN * kBK * 4;  // one of hi / lo
   static constexpr uint32_t kStageBytes = 2 * kPlaneBytes;
-  static constexpr bool kSplitN = CTB_TM_SPLIT_N && BN == 64;
-  static constexpr uint32_t kAccCols = kSplitN ? 3 * BN : BN;  // one accumulator buffer
-  static constexpr uint32_t kAColumn0 = 2 * kAccCols;  // first activation stage column
+  static constexpr bool kSplitN = (CTB_TM_SPLIT_N && BN == 64) || (CTB_TM_SPLIT_N128 && BN == 128);
+  static constexpr uint32_t kAccCols = kSplitN ? 2 * BN : BN;  // one accumulator buffer
+  static constexpr int kAccBufs = kAccCols * 2 <= 256 ? 2 : 1;   // double-buffered when it fits
+  static constexpr uint32_t kAColumn0 = kAccBufs * kAccCols;    // first activation stage column
   static constexpr int kAStages = (kTmemCols - kAColumn0) / (2 * kBK);
   static_assert(kAStages <= kMaxStages && kAStages % 2 == 0, "activation stages (one gather group each)");
   static_assert(kStages * kStageBytes <= kStageRegionBytes, "shared memory budget");
@@ -657,8 +664,9 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     int g = 0;
     bool ok = true;
     for (int local = 0; local < my_tiles && ok; ++local) {
-      const int buf = local & 1;
-      if (local >= 2 && !mbar_wait(&bars->tmem_empty[buf], ((local >> 1) - 1) & 1, abort, scratch, 33)) {
+      const int buf = local % T::kAccBufs;
+      const int buf_use = local / T::kAccBufs;
+      if (buf_use > 0 && !mbar_wait(&bars->tmem_empty[buf], (buf_use - 1) & 1, abort, scratch, 33)) {
         ok = false;
         break;
       }
@@ -685,7 +693,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
             // [B_hi; B_lo] as one 128-row operand: b_lo(s) follows b_hi(s).
             constexpr uint32_t idesc_wide = instr_desc(kFormatTF32, kBM, 2 * BN);
             umma_tf32_ts(acc, ahi + 8 * kk, bhi + dk, idesc_wide, (kb | kk) != 0);
-            umma_tf32_ts(acc + 2 * BN, alo + 8 * kk, bhi + dk, idesc, (kb | kk) != 0);
+            umma_tf32_ts(acc, alo + 8 * kk, bhi + dk, idesc, 1);
           } else {
             umma_tf32_ts(acc, ahi + 8 * kk, bhi + dk, idesc, (kb | kk) != 0);
             umma_tf32_ts(acc, ahi + 8 * kk, blo + dk, idesc, 1);
@@ -751,9 +759,6 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       if (T::kSplitN) {
         uint32_t t[32];
         tmem_load_32x32(taddr + BN + 32 * ci, t);  // A_hi . B_lo
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(t[j]));
-        tmem_load_32x32(taddr + 2 * BN + 32 * ci, t);  // A_lo . B_hi
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(t[j]));
       }
@@ -836,12 +841,12 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       }
       int local = 0;
       for (; local < my_tiles; ++local) {
-        const int buf = local & 1;
+        const int buf = local % T::kAccBufs;
         const long long tile = tile_index(local);
         const int co0 = static_cast<int>(tile % co_tiles) * BN;
         const TileSpan tile_span = span_of(tile);
         load_params(co0);
-        const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
+        const bool ready = mbar_wait(&bars->tmem_full[buf], (local / T::kAccBufs) & 1, abort, scratch, 37);
         // The four warps of a half leave together (they share named barriers).
         if (epilogue_any(half, !ready)) break;
         tc_fence_after_sync();
@@ -911,7 +916,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       // come here. Plain loads and stores, kept small so the variant's common
       // path does not pay for this one in registers.
       for (int local = 0; local < my_tiles; ++local) {
-        const int buf = local & 1;
+        const int buf = local % T::kAccBufs;
         const long long tile = tile_index(local);
         const int co0 = static_cast<int>(tile % co_tiles) * BN;
         const long long pixel = tile_p0(tile / co_tiles) + quarter * 32 + lane;
@@ -922,7 +927,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
           base = img * p.k * pixels_per_image + (pixel - img * pixels_per_image);
         }
         load_params(co0);
-        const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
+        const bool ready = mbar_wait(&bars->tmem_full[buf], (local / T::kAccBufs) & 1, abort, scratch, 37);
         if (epilogue_any(half, !ready)) break;
         tc_fence_after_sync();
         const uint32_t taddr = tmem + buf * T::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -989,7 +994,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
 #pragma unroll
       for (int ci = 0; ci < kChunks; ++ci) prefetch_residual(0, ci);
       for (int local = 0; local < my_tiles; ++local) {
-        const int buf = local & 1;
+        const int buf = local % T::kAccBufs;
         const long long tile = tile_index(local);
         const int co0 = static_cast<int>(tile % co_tiles) * BN;
         const long long pixel = tile_p0(tile / co_tiles) + quarter * 32 + lane;
@@ -1000,7 +1005,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
           base = img * p.k * pixels_per_image + (pixel - img * pixels_per_image);
         }
         load_params(co0);
-        const bool ready = mbar_wait(&bars->tmem_full[buf], (local >> 1) & 1, abort, scratch, 37);
+        const bool ready = mbar_wait(&bars->tmem_full[buf], (local / T::kAccBufs) & 1, abort, scratch, 37);
         if (epilogue_any(half, !ready)) break;
         tc_fence_after_sync();
         const uint32_t taddr = tmem + buf * T::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
