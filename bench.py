@@ -412,7 +412,10 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
     batch = args.batch
     weights = workloads.resnet50_weights("baseline", seed=0)
     model = workloads.build_resnet50(weights, batch=batch)
-    engine = ct.build_engine(model, device_id=local, enable_cuda_graph=True, enable_profiling=True,
+    # The headline runs without per-op profiling events (as a user would run
+    # it); a second engine with profiling gives the per-op conv times for the
+    # roofline afterwards, outside the timed region.
+    engine = ct.build_engine(model, device_id=local, enable_cuda_graph=True, enable_profiling=False,
                              enable_residual_fusion=True, tuning_mode=ct.TUNING_DISABLED)
     ctx = engine.create_context()
     x_host = workloads.resnet50_input(batch, seed=rank)
@@ -426,9 +429,6 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
         ctx.synchronize()
 
     launches = kernel_launches_per_run(engine, ctx)
-    op_types = [o["op_type"] for o in engine.ops()]
-    conv_ops = [i for i, t in enumerate(op_types) if "Conv" in t]
-    conv_ms = []
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         barrier(world)
@@ -437,13 +437,28 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
         for _ in range(args.steps):
             ctx.run_async(stream.cuda_stream)
             ctx.synchronize()  # the reference harness synchronizes every run
-            events = ctx.profile_events()
-            conv_ms.append(sum(events[i][1] for i in conv_ops))
         end.record(stream)
         torch.cuda.synchronize()
         barrier(world)
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
     clock_summary = clocks.summary()
+
+    # Per-op conv times (engine profiler: CUDA events around each op).
+    prof_engine = ct.build_engine(model, device_id=local, enable_cuda_graph=True, enable_profiling=True,
+                                  enable_residual_fusion=True, tuning_mode=ct.TUNING_DISABLED)
+    prof_ctx = prof_engine.create_context()
+    prof_ctx.bind_tensor("input", x)
+    prof_ctx.bind_tensor("output", y, output=True)
+    op_types = [o["op_type"] for o in prof_engine.ops()]
+    conv_ops = [i for i, t in enumerate(op_types) if "Conv" in t]
+    conv_ms = []
+    for step in range(3 + min(args.steps, 5)):
+        prof_ctx.run_async(stream.cuda_stream)
+        prof_ctx.synchronize()
+        if step >= 3:
+            events = prof_ctx.profile_events()
+            conv_ms.append(sum(events[i][1] for i in conv_ops))
+    del prof_ctx, prof_engine
     ms_per_step = elapsed_ms / args.steps
     value = world * batch * args.steps / (elapsed_ms / 1e3)
 

@@ -388,6 +388,26 @@ class InvocationKernel final : public OpKernel {
       grid[axis] = static_cast<unsigned int>(extent);
     }
     const auto& a = invocation_.artifact;
+    if (a.programmatic_launch) {
+      // The kernel waits for its predecessor itself (griddepcontrol.wait), so
+      // its CTAs may start on SMs the previous kernel has already left.
+      CUlaunchAttribute attribute{};
+      attribute.id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+      attribute.value.programmaticStreamSerializationAllowed = 1;
+      CUlaunchConfig config{};
+      config.gridDimX = grid[0];
+      config.gridDimY = grid[1];
+      config.gridDimZ = grid[2];
+      config.blockDimX = static_cast<unsigned int>(a.num_warps * 32);
+      config.blockDimY = 1;
+      config.blockDimZ = 1;
+      config.sharedMemBytes = static_cast<unsigned int>(a.shared_memory_bytes);
+      config.hStream = reinterpret_cast<CUstream>(context->stream);
+      config.attrs = &attribute;
+      config.numAttrs = 1;
+      return drv::Check(drv::Get().cuLaunchKernelEx(&config, function_, params_.pointers.data(), nullptr),
+                        "cuLaunchKernelEx");
+    }
     return drv::Check(drv::Get().cuLaunchKernel(function_, grid[0], grid[1], grid[2],
                                                 static_cast<unsigned int>(a.num_warps * 32), 1, 1,
                                                 static_cast<unsigned int>(a.shared_memory_bytes),

@@ -337,6 +337,7 @@ Status ArtifactRepository::Load(const std::vector<std::string>& paths) {
         a.num_warps = AsInt(entry.at("num_warps"));
         a.num_stages = AsInt(entry.at("num_stages"));
         a.shared_memory_bytes = AsInt(entry.at("shared_memory_bytes"));
+        a.programmatic_launch = a.binary_format == "cubin" && IntOr(entry, "programmatic_launch", 0) != 0;
         if (a.num_warps <= 0 || a.num_warps > 32) throw std::runtime_error("num_warps must be 1..32");
         if (a.shared_memory_bytes < 0 || a.shared_memory_bytes > 232448) {
           throw std::runtime_error("shared_memory_bytes exceeds the sm_100 limit");

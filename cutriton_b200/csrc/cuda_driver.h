@@ -38,6 +38,7 @@ namespace drv {
   X(cuModuleGetFunction)             \
   X(cuFuncSetAttribute)              \
   X(cuLaunchKernel)                  \
+  X(cuLaunchKernelEx)                \
   X(cuStreamCreate)                  \
   X(cuStreamDestroy)                 \
   X(cuStreamSynchronize)             \

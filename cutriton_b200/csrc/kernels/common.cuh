@@ -10,6 +10,18 @@
 #include <stdint.h>
 
 #define CTB_RESERVED_PARAMS void* runtime_scratch, void* profile_scratch
+// Programmatic dependent launch. Every pack kernel (launched with
+// programmatic stream serialization, see cuda_launcher.cpp) first lets the
+// next kernel start launching, then waits until the preceding kernel in the
+// stream has completed and its writes are visible. Nothing before the wait
+// may touch activation memory (reads or writes): only shared memory, TMEM and
+// kernel parameters. Without the launch attribute both are no-ops.
+#define CTB_GRID_DEPENDENCY_SYNC()                                      \
+  do {                                                                  \
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");     \
+    asm volatile("griddepcontrol.wait;" ::: "memory");                  \
+  } while (0)
+
 #define CTB_UNUSED_RESERVED() \
   do {                        \
     (void)runtime_scratch;    \

@@ -142,6 +142,7 @@ __device__ __forceinline__ void conv_simt(const float* __restrict__ x, const flo
 extern "C" __global__ void __launch_bounds__(kThreads)
 ctb_conv_f32_simt(const float* x, const float* weight, float* output, CTB_CONV_DIMS, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   conv_simt<kPlain>(x, weight, nullptr, nullptr, nullptr, nullptr, nullptr, output, CTB_CONV_SHAPE, 0.0f);
 }
 
@@ -150,6 +151,7 @@ ctb_conv_bn_f32_simt(const float* x, const float* weight, const float* scale, co
                      const float* mean, const float* variance, float* output, CTB_CONV_DIMS, float epsilon,
                      CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   conv_simt<kBatchNorm>(x, weight, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE, epsilon);
 }
 
@@ -158,6 +160,7 @@ ctb_conv_bn_relu_f32_simt(const float* x, const float* weight, const float* scal
                           const float* mean, const float* variance, float* output, CTB_CONV_DIMS,
                           float epsilon, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   conv_simt<kBatchNormRelu>(x, weight, scale, bias, mean, variance, nullptr, output, CTB_CONV_SHAPE, epsilon);
 }
 
@@ -166,6 +169,7 @@ ctb_conv_bn_add_relu_f32_simt(const float* x, const float* weight, const float* 
                               const float* mean, const float* variance, const float* residual, float* output,
                               CTB_CONV_DIMS, float epsilon, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   conv_simt<kBatchNormAddRelu>(x, weight, scale, bias, mean, variance, residual, output, CTB_CONV_SHAPE, epsilon);
 }
 
@@ -174,6 +178,7 @@ extern "C" __global__ void __launch_bounds__(kThreads)
 ctb_gemm_f32_simt(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ output, int m,
                   int n, int k, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   __shared__ float As[kBK][kBM];
   __shared__ float Bs[kBK][kBN + 1];
   const int tid = threadIdx.x;

@@ -182,6 +182,8 @@ __device__ __forceinline__ void conv_tc(const TmaDescriptor* tma_w, const float*
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = bars->tmem_base;
+  // Activations are touched only after the preceding kernel has finished.
+  CTB_GRID_DEPENDENCY_SYNC();
 
   if (warp >= kGatherWarp0) {
     // ---- gather: one thread per output pixel of the tile ----

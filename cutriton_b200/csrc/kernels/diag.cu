@@ -14,6 +14,7 @@
 extern "C" __global__ void __launch_bounds__(256)
 ctb_bounded_wait_probe_f32(const float* x, float* output, int numel, int limit_us, CTB_RESERVED_PARAMS) {
   (void)profile_scratch;
+  CTB_GRID_DEPENDENCY_SYNC();
   using namespace ctb::tc;
   __shared__ uint64_t never_completed;
   __shared__ int abort;

@@ -74,18 +74,21 @@ __device__ __forceinline__ void binary_f32(const float* __restrict__ a, const fl
 extern "C" __global__ void __launch_bounds__(kThreads)
 ctb_relu_f32(const float* x, float* out, int total, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   unary_f32(x, out, total, Relu{});
 }
 
 extern "C" __global__ void __launch_bounds__(kThreads)
 ctb_add_f32(const float* a, const float* b, float* out, int total, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   binary_f32(a, b, out, total, Add{});
 }
 
 extern "C" __global__ void __launch_bounds__(kThreads)
 ctb_add_relu_f32(const float* a, const float* b, float* out, int total, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   binary_f32(a, b, out, total, AddRelu{});
 }
 
@@ -96,6 +99,7 @@ ctb_batch_norm_f32(const float* x, const float* scale, const float* bias, const 
                    const float* variance, float* out, int total, int channels, int spatial,
                    float epsilon, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   auto affine = [&](float v, int c) {
     return (v - mean[c]) * rsqrtf(variance[c] + epsilon) * scale[c] + bias[c];
   };
@@ -125,6 +129,7 @@ ctb_batch_norm_f32(const float* x, const float* scale, const float* bias, const 
 extern "C" __global__ void __launch_bounds__(kThreads)
 ctb_gelu_f16(const __half* x, __half* out, int total, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   const long long base = static_cast<long long>(blockIdx.x) * kChunkF16;
   if (base + kChunkF16 <= total && ctb::aligned16(x) && ctb::aligned16(out)) {
     uint4 v[kVecPerThread];
@@ -152,6 +157,7 @@ ctb_gelu_f16(const __half* x, __half* out, int total, CTB_RESERVED_PARAMS) {
 extern "C" __global__ void __launch_bounds__(kThreads)
 ctb_add_f16(const __half* a, const __half* b, __half* out, int total, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   const long long base = static_cast<long long>(blockIdx.x) * kChunkF16;
   if (base + kChunkF16 <= total && ctb::aligned16(a) && ctb::aligned16(b) && ctb::aligned16(out)) {
     uint4 va[kVecPerThread], vb[kVecPerThread];

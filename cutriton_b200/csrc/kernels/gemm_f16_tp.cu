@@ -111,6 +111,8 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = bars->tmem_base;
+  // Activations are touched only after the preceding kernel has finished.
+  CTB_GRID_DEPENDENCY_SYNC();
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----

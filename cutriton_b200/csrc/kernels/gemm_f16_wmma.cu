@@ -108,6 +108,7 @@ __device__ __forceinline__ void gemm_wmma(const __half* __restrict__ a, const __
 extern "C" __global__ void __launch_bounds__(kThreads)
 ctb_gemm_f16_wmma(const __half* a, const __half* b, __half* output, int m, int n, int k, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   gemm_wmma<false>(a, b, output, m, n, k);
 }
 
@@ -115,5 +116,6 @@ extern "C" __global__ void __launch_bounds__(kThreads)
 ctb_gemm_gelu_f16_wmma(const __half* a, const __half* b, __half* output, int m, int n, int k,
                        CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   gemm_wmma<true>(a, b, output, m, n, k);
 }

@@ -120,6 +120,7 @@ extern "C" __global__ void __launch_bounds__(256)
 ctb_layer_norm_f16(const __half* x, const __half* scale, const __half* bias, __half* out, int rows,
                    int columns, float epsilon, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (row >= rows) return;
   const long long offset = static_cast<long long>(row) * columns;
@@ -137,6 +138,7 @@ extern "C" __global__ void __launch_bounds__(256)
 ctb_skip_layer_norm_f16(const __half* x, const __half* residual, const __half* scale, const __half* bias,
                         __half* out, int rows, int columns, float epsilon, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (row >= rows) return;
   const long long offset = static_cast<long long>(row) * columns;
@@ -160,6 +162,7 @@ ctb_skip_layer_norm_f16(const __half* x, const __half* residual, const __half* s
 extern "C" __global__ void __launch_bounds__(256)
 ctb_softmax_f16(const __half* x, __half* out, int rows, int columns, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (row >= rows) return;
   const int lane = threadIdx.x & 31;

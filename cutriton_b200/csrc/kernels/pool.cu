@@ -19,6 +19,7 @@ ctb_max_pool_f32(const float* __restrict__ x, float* __restrict__ out, int n, in
                  int out_h, int out_w, int kernel_h, int kernel_w, int stride_h, int stride_w,
                  int pad_h, int pad_w, int dilation_h, int dilation_w, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   const long long total = static_cast<long long>(n) * c * out_h * out_w;
   const long long index = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (index >= total) return;
@@ -46,6 +47,7 @@ extern "C" __global__ void __launch_bounds__(256)
 ctb_global_average_pool_f32(const float* __restrict__ x, float* __restrict__ out, int n, int c, int h,
                             int w, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   const int warps_per_block = blockDim.x / 32;
   const long long plane = static_cast<long long>(blockIdx.x) * warps_per_block + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -68,6 +70,7 @@ extern "C" __global__ void __launch_bounds__(256)
 ctb_max_pool_3x3s2_f32(const float* __restrict__ x, float* __restrict__ out, int n, int c, int h, int w,
                        int out_h, int out_w, CTB_RESERVED_PARAMS) {
   CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
   const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= static_cast<long long>(n) * c * out_h) return;  // warp-uniform

@@ -145,6 +145,11 @@ struct KernelArtifact {
   std::array<GridExpression, 3> launch_grid{};
   std::unordered_map<std::string, int64_t> launch_meta;
   int grid_divisor{1};
+  // sm_100a extension: the kernel waits for the preceding grid itself
+  // (griddepcontrol.wait before touching activations), so it may be launched
+  // with programmatic stream serialization and overlap the previous kernel's
+  // tail.
+  bool programmatic_launch{false};
   std::vector<KernelArgumentSpec> arguments;
   std::vector<KernelConstraint> constraints;
   std::string identity() const { return pack_name + ":" + kernel_id + ":" + variant_id; }
