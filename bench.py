@@ -46,7 +46,7 @@ FFN = dict(tokens=4096, hidden=768, inner=3072)
 def parse_args() -> argparse.Namespace:
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=RN_BATCH_PER_GPU, help="images per GPU")
@@ -268,7 +268,8 @@ def load_peaks() -> tuple[dict, str]:
 
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons during the
-    timed region (200 ms period)."""
+    timed region (100 ms period); entering waits for the first sample so the
+    samples fall inside the region rather than in nvidia-smi's start-up."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -283,10 +284,16 @@ class ClockSampler:
         try:
             self.out = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.device_index), "-lms", "200"], stdout=self.out,
+                                          "-i", str(self.device_index), "-lms", "100"], stdout=self.out,
                                          stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
+            return self
+        deadline = time.monotonic() + 5.0
+        while time.monotonic() < deadline and self.proc.poll() is None:
+            if self.path.stat().st_size > 0:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
@@ -490,23 +497,55 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
 
     if not args.no_e2e:
         pinned = torch.from_numpy(x_host).pin_memory()
-        host_out = np.empty((batch, 1000), np.float32)
         host_in = pinned.numpy()
-        ctx.run_host({"input": host_in}, {"output": host_out}, stream=stream.cuda_stream)
+        host_outs = [torch.empty(batch, 1000).pin_memory().numpy() for _ in range(2)]
+        steps = max(6, args.steps)
+        # Serial: one context, each call waits for its own copies.
+        ctx.run_host({"input": host_in}, {"output": host_outs[0]}, stream=stream.cuda_stream)
         barrier(world)
         torch.cuda.synchronize()
         e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e_start.record(stream)
-        steps = max(3, args.steps // 2)
         for _ in range(steps):
-            ctx.run_host({"input": host_in}, {"output": host_out}, stream=stream.cuda_stream)
+            ctx.run_host({"input": host_in}, {"output": host_outs[0]}, stream=stream.cuda_stream)
         e_end.record(stream)
         torch.cuda.synchronize()
         barrier(world)
+        serial_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+        # Pipelined: two contexts of the engine on two streams; step i+1's
+        # host->device copy runs under step i's kernels.
+        ctx2 = engine.create_context()
+        ctx2.bind_tensor("input", torch.empty_like(x))
+        ctx2.bind_tensor("output", torch.empty_like(y), output=True)
+        stream2 = torch.cuda.Stream(device=device)
+        ctxs, streams = [ctx, ctx2], [stream, stream2]
+        for j in range(2):
+            ctxs[j].run_host({"input": host_in}, {"output": host_outs[j]}, stream=streams[j].cuda_stream)
+        barrier(world)
+        torch.cuda.synchronize()
+        e_start.record(stream)
+        stream2.wait_event(e_start)
+        for i in range(steps):
+            j = i % 2
+            if i >= 2:
+                ctxs[j].synchronize()
+            ctxs[j].run_host_async({"input": host_in}, {"output": host_outs[j]}, streams[j].cuda_stream)
+        tail = torch.cuda.Event()
+        tail.record(stream2)
+        stream.wait_event(tail)
+        e_end.record(stream)
+        for c in ctxs:
+            c.synchronize()
+        torch.cuda.synchronize()
+        barrier(world)
         e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+        del ctx2
         result["e2e"] = {"value": world * batch * steps / (e_ms / 1e3), "unit": "img/s",
-                         "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(host_out.nbytes),
-                         "path": "ctb_context_run_host (C ABI), pinned host buffers"}
+                         "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(host_outs[0].nbytes),
+                         "steps": steps,
+                         "path": "ctb_context_run_host_async (C ABI): two contexts on two streams, pinned host buffers",
+                         "serial_value": world * batch * steps / (serial_ms / 1e3),
+                         "serial_path": "ctb_context_run_host (C ABI), one context, waits every step"}
     return result
 
 

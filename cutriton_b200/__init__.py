@@ -103,6 +103,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ctb_context_selected_candidate": (ctypes.c_int, [_P, ctypes.c_int]),
     "ctb_context_select_candidate": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int]),
     "ctb_context_run_host": (ctypes.c_int, [_P, ctypes.c_int, _CHARPP, ctypes.POINTER(_P), ctypes.c_int, _CHARPP, ctypes.POINTER(_P), _P]),
+    "ctb_context_run_host_async": (ctypes.c_int, [_P, ctypes.c_int, _CHARPP, ctypes.POINTER(_P), ctypes.c_int, _CHARPP, ctypes.POINTER(_P), _P]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -340,12 +341,28 @@ class ExecutionContext:
 
     def run_host(self, inputs: dict[str, np.ndarray], outputs: dict[str, np.ndarray], stream: int | None = None) -> None:
         """Host -> device copies, run, device -> host copies in one call."""
+        self._run_host(library().ctb_context_run_host, inputs, outputs, stream or 0)
+
+    def run_host_async(self, inputs: dict[str, np.ndarray], outputs: dict[str, np.ndarray], stream: int) -> None:
+        """The same copies and run enqueued on `stream`; returns without waiting.
+
+        The arrays must stay alive (and pinned, for the copies to overlap) until
+        synchronize().
+        """
+        if not stream:
+            raise ValueError("run_host_async needs a stream")
+        self._run_host(library().ctb_context_run_host_async, inputs, outputs, stream)
+
+    def _run_host(self, fn, inputs: dict[str, np.ndarray], outputs: dict[str, np.ndarray], stream: int) -> None:
+        for name, arr in list(inputs.items()) + list(outputs.items()):
+            if not arr.flags["C_CONTIGUOUS"]:
+                raise ValueError(f"host buffer {name!r} must be C-contiguous")
         in_names = list(inputs)
         out_names = list(outputs)
         in_ptrs = (_P * max(1, len(in_names)))(*[inputs[n].ctypes.data for n in in_names])
         out_ptrs = (_P * max(1, len(out_names)))(*[outputs[n].ctypes.data for n in out_names])
-        _check(library().ctb_context_run_host(self._h, len(in_names), _strings(in_names), in_ptrs, len(out_names),
-                                              _strings(out_names), out_ptrs, _P(stream or 0)))
+        _check(fn(self._h, len(in_names), _strings(in_names), in_ptrs, len(out_names), _strings(out_names), out_ptrs,
+                  _P(stream)))
 
 
 def exported_symbols() -> Iterable[str]:

@@ -386,10 +386,17 @@ int ctb_context_select_candidate(ctb_context c, int op, int candidate) {
   return Report(c->context->SelectCandidate(static_cast<std::size_t>(op), static_cast<std::size_t>(candidate)));
 }
 
-int ctb_context_run_host(ctb_context c, int num_inputs, const char* const* input_names,
-                         const void* const* host_inputs, int num_outputs, const char* const* output_names,
-                         void* const* host_outputs, void* stream) {
+namespace {
+
+// H2D copies of the inputs, the run, D2H copies of the outputs. With a stream
+// everything is enqueued on it and the run stays pending (the caller
+// synchronizes); without one the copies are synchronous around a synchronous
+// run on the context stream.
+int EnqueueRunHost(ctb_context c, int num_inputs, const char* const* input_names, const void* const* host_inputs,
+                   int num_outputs, const char* const* output_names, void* const* host_outputs, void* stream,
+                   bool wait) {
   if (c == nullptr || num_inputs < 0 || num_outputs < 0) return Invalid("invalid arguments");
+  if (c->context->run_pending()) return Report(Status::RuntimeError("a run is already pending"));
   Status status = drv::Ensure();
   if (!status.ok()) return Report(status);
   const auto& api = drv::Get();
@@ -412,8 +419,6 @@ int ctb_context_run_host(ctb_context c, int num_inputs, const char* const* input
     *bytes = it->second.desc().ByteSize();
     return Status::OK();
   };
-  // With a stream every copy and the run are ordered on it; without one the
-  // copies are synchronous around a synchronous run on the context stream.
   const CUstream s = reinterpret_cast<CUstream>(stream);
   for (int i = 0; i < num_inputs; ++i) {
     CUdeviceptr ptr{};
@@ -444,7 +449,24 @@ int ctb_context_run_host(ctb_context c, int num_inputs, const char* const* input
       return Report(status);
     }
   }
-  return Report(s != nullptr ? c->context->Synchronize() : Status::OK());
+  return Report(s != nullptr && wait ? c->context->Synchronize() : Status::OK());
+}
+
+}  // namespace
+
+int ctb_context_run_host(ctb_context c, int num_inputs, const char* const* input_names,
+                         const void* const* host_inputs, int num_outputs, const char* const* output_names,
+                         void* const* host_outputs, void* stream) {
+  return EnqueueRunHost(c, num_inputs, input_names, host_inputs, num_outputs, output_names, host_outputs, stream,
+                        true);
+}
+
+int ctb_context_run_host_async(ctb_context c, int num_inputs, const char* const* input_names,
+                               const void* const* host_inputs, int num_outputs, const char* const* output_names,
+                               void* const* host_outputs, void* stream) {
+  if (stream == nullptr) return Invalid("ctb_context_run_host_async needs a stream");
+  return EnqueueRunHost(c, num_inputs, input_names, host_inputs, num_outputs, output_names, host_outputs, stream,
+                        false);
 }
 
 }  // extern "C"

@@ -57,6 +57,7 @@ class ExecutionContext {
   // Waits for the pending run, collects profiling events and checks the
   // device-side error word of the kernels (bounded waits that expired).
   Status Synchronize();
+  bool run_pending() const { return run_pending_; }
 
   const Profiler& profiler() const { return profiler_; }
   std::size_t cached_cuda_graph_count() const;

@@ -162,6 +162,14 @@ int ctb_context_select_candidate(ctb_context context, int op, int candidate);
 int ctb_context_run_host(ctb_context context, int num_inputs, const char* const* input_names,
                          const void* const* host_inputs, int num_outputs,
                          const char* const* output_names, void* const* host_outputs, void* stream);
+/* Same copies and run, enqueued on `stream` (required), returning without
+ * waiting: the run stays pending until ctb_context_synchronize. Host buffers
+ * must be pinned for the copies to overlap other work and must stay valid
+ * until then. Two contexts of one engine on two streams pipeline one step's
+ * copies under the other's kernels. */
+int ctb_context_run_host_async(ctb_context context, int num_inputs, const char* const* input_names,
+                               const void* const* host_inputs, int num_outputs,
+                               const char* const* output_names, void* const* host_outputs, void* stream);
 
 #ifdef __cplusplus
 }

@@ -255,3 +255,34 @@ def test_run_host_matches_device_run(cuda):
     ctx.run_host({"x": x}, {"output": host_out2}, stream=stream.cuda_stream)
     assert np.array_equal(host_out, host_out2)
     assert np.array_equal(host_out, dy.cpu().numpy())
+
+
+def test_run_host_async_two_contexts_pipeline(cuda):
+    """Two contexts of one engine on two streams, each step enqueued without waiting."""
+    import torch
+
+    w = workloads.ffn_weights(256, 1024, seed=6)
+    model = workloads.build_ffn(w, 32, 256, 1024)
+    engine = ct.build_engine(model, tuning_mode=ct.TUNING_DISABLED)
+    ctxs, streams = [], []
+    for _ in range(2):
+        ctx = engine.create_context()
+        ctx.bind_tensor("x", torch.empty(32, 256, dtype=torch.float16, device=cuda))
+        ctx.bind_tensor("output", torch.empty(32, 256, dtype=torch.float16, device=cuda), output=True)
+        ctxs.append(ctx)
+        streams.append(torch.cuda.Stream())
+    xs = [torch.from_numpy(workloads.ffn_input(32, 256, seed=10 + i)).pin_memory() for i in range(4)]
+    outs = [torch.zeros(32, 256, dtype=torch.float16).pin_memory() for _ in range(4)]
+    for i in range(4):
+        j = i % 2
+        if i >= 2:
+            ctxs[j].synchronize()
+        ctxs[j].run_host_async({"x": xs[i].numpy()}, {"output": outs[i].numpy()}, streams[j].cuda_stream)
+    for ctx in ctxs:
+        ctx.synchronize()
+    for i in range(4):
+        expected = np.zeros((32, 256), np.float16)
+        ctxs[0].run_host({"x": xs[i].numpy()}, {"output": expected})
+        assert np.array_equal(outs[i].numpy(), expected)
+    with pytest.raises(ValueError):
+        ctxs[0].run_host_async({"x": xs[0].numpy()}, {"output": outs[0].numpy()}, 0)
