@@ -7,20 +7,22 @@
 // K-major and staged by TMA in the 128-byte-swizzled layout the UMMA
 // descriptors read.
 //
-// One CTA per SM walks the 128 x BN output tiles (BN = 256, or 128 when
-// 256-wide tiles would leave SMs idle) in a static round-robin, N fastest so
-// co-running CTAs share the A tile in L2. Roles (10 warps):
+// One CTA per SM walks the 128 x BN output tiles (BN = 256, or 128 when that
+// saves enough waves on a small problem) in a static round-robin, N fastest so
+// co-running CTAs share the A tile in L2. Roles (18 warps):
 //   warp 0 lane 0 — TMA producer: A (128 x 64) and B (BN x 64) per k block
 //       through a STAGES-deep shared-memory ring (full / empty barriers);
 //   warp 1 lane 0 — UMMA issuer: 4 x (128 x BN x 16) per k block into one of
 //       two TMEM accumulators (2 x BN columns), so the epilogue of one tile
 //       overlaps the MMAs of the next;
-//   warps 2-9 — epilogue, two warps per TMEM lane quarter (warp % 4 = 32
-//       rows), each taking half of the columns, 64 at a time -> GELU -> FP16
-//       -> a 32 x 64 staging box in shared memory (128-byte swizzle,
+//   warps 2-17 — epilogue, four warps per TMEM lane quarter (warp % 4 = 32
+//       rows), each taking a quarter of the columns, 32 at a time -> GELU ->
+//       FP16 -> a 32 x 32 staging box in shared memory (64-byte swizzle,
 //       conflict-free 16-byte writes) -> TMA tensor store; each warp hands its
-//       half of the accumulator back as soon as it is in registers. Eight
-//       warps keep the erf-GELU of one tile shorter than the next tile's MMAs.
+//       columns of the accumulator back as soon as they are in registers.
+//       The erf-GELU is latency-bound (two MUFU ops in a dependent chain per
+//       element): sixteen warps, four per scheduler, hide it where eight
+//       left the epilogue of a tile longer than the next tile's MMAs.
 // All waits are bounded (tc_common.cuh).
 
 #include "tc_common.cuh"
@@ -31,13 +33,16 @@ using namespace ctb::tc;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // FP16 elements per 128-byte swizzle row
-constexpr int kThreads = 320;
-constexpr int kEpilogueWarps = 8;
+constexpr int kEpilogueWarps = 16;
+constexpr int kThreads = (2 + kEpilogueWarps) * 32;
+// Columns per staging chunk: 32 FP16 = 64-byte rows, stored through a
+// 64-byte-swizzled 32 x 32 TMA box.
+constexpr int kChunk = 32;
 constexpr int kEpilogueWarp0 = 2;
 constexpr uint32_t kTileA = kBM * kBK * 2;      // 16 KB
 constexpr uint32_t kBoxRowsB = 128;              // B rows (N) per TMA box
 constexpr uint32_t kRingBytes = 196608;          // 4 x (16 + 32) KB = 6 x (16 + 16) KB
-constexpr uint32_t kStageBoxBytes = 32 * 128;    // 32 rows x 64 FP16 (one store box)
+constexpr uint32_t kStageBoxBytes = 32 * kChunk * 2;  // 2 KB: 32 rows x 32 FP16
 constexpr uint32_t kStagingBytes = kEpilogueWarps * kStageBoxBytes;
 constexpr int kMaxStages = 6;
 
@@ -182,9 +187,11 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
       mbar_wait(&bars->drain, 0, &never, scratch, 54);
     }
   } else if (warp >= kEpilogueWarp0) {
-    // ---- epilogue: rows quarter*32 + lane, columns [c_begin, c_begin + BN/2) ----
+    // ---- epilogue: rows quarter*32 + lane, columns [c_begin, c_begin + BN/4) ----
+    constexpr int kSpan = BN / (kEpilogueWarps / 4);
+    constexpr int kPacks = kChunk / 8;
     const int quarter = warp & 3;
-    const int c_begin = ((warp - kEpilogueWarp0) / 4) * (BN / 2);
+    const int c_begin = ((warp - kEpilogueWarp0) / 4) * kSpan;
     uint8_t* box = staging + (warp - kEpilogueWarp0) * kStageBoxBytes;
     bool box_used = false;
     for (int local = 0; local < my_tiles; ++local) {
@@ -199,19 +206,18 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
       const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
       const int row = m0 + quarter * 32 + lane;
 #pragma unroll 1
-      for (int c = c_begin; c < c_begin + BN / 2; c += 64) {
-        uint32_t v[64];
-        tmem_load_32x32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_load_32x32(taddr + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-        if (c + 64 == c_begin + BN / 2) {
+      for (int c = c_begin; c < c_begin + kSpan; c += kChunk) {
+        uint32_t v[kChunk];
+        tmem_load_32x32(taddr + c, v);
+        if (c + kChunk == c_begin + kSpan) {
           // This warp's columns of the accumulator are in registers: hand them back.
           tc_fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
         }
-        uint4 packed[8];
+        uint4 packed[kPacks];
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
+        for (int ch = 0; ch < kPacks; ++ch) {
           __half2* h = reinterpret_cast<__half2*>(&packed[ch]);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -230,10 +236,10 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
             if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             __syncwarp();
           }
-          // Row `lane` (128 bytes), 16-byte chunk j at chunk j ^ (lane % 8).
+          // Row `lane` (64 bytes); 64-byte swizzle: 16-byte chunk j at j ^ ((lane / 2) % 4).
 #pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            *reinterpret_cast<uint4*>(box + lane * 128 + (((ch ^ lane) & 7) << 4)) = packed[ch];
+          for (int ch = 0; ch < kPacks; ++ch) {
+            *reinterpret_cast<uint4*>(box + lane * 64 + (((ch ^ (lane >> 1)) & 3) << 4)) = packed[ch];
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
@@ -245,7 +251,7 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
         } else if (row < m) {
           __half* dst = out + static_cast<long long>(row) * n + n0 + c;
 #pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
+          for (int ch = 0; ch < kPacks; ++ch) {
             if (n0 + c + ch * 8 < n) *reinterpret_cast<uint4*>(dst + ch * 8) = packed[ch];
           }
         }
@@ -270,8 +276,13 @@ __device__ __forceinline__ void gemm_tp_dispatch(const TmaDescriptor* tma_a, con
   // 1024-byte alignment for the 128-byte swizzle atoms.
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const long long m_tiles = (m + kBM - 1) / kBM;
-  // 256-wide tiles unless that leaves fewer than two waves of tiles.
-  if (m_tiles * ((n + 255) / 256) >= 2 * static_cast<long long>(gridDim.x)) {
+  // Waves of 256- vs 128-wide tiles; a 128-wide tile costs ~0.69 of a
+  // 256-wide one at steady state (measured), so 128 wins only when it saves
+  // enough waves (small problems).
+  const long long g = gridDim.x;
+  const long long w256 = (m_tiles * ((n + 255) / 256) + g - 1) / g;
+  const long long w128 = (m_tiles * ((n + 127) / 128) + g - 1) / g;
+  if (100 * w256 <= 69 * w128) {
     gemm_tp<kGelu, 256>(smem, tma_a, tma_b, tma_out, out, m, n, k, scratch);
   } else {
     gemm_tp<kGelu, 128>(smem, tma_a, tma_b, tma_out, out, m, n, k, scratch);

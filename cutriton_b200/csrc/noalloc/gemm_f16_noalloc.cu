@@ -68,15 +68,18 @@ int FailCuda(char* error, size_t error_len, const char* what, cudaError_t status
   return Fail(error, error_len, CTB_NOALLOC_CUDA_ERROR, message);
 }
 
-// Row-major [rows, cols] FP16 matrix, box {64 columns, box_rows rows}, 128-byte swizzle.
-bool EncodeFp16(CUtensorMap* map, const void* base, int rows, int cols, int box_rows) {
+// Row-major [rows, cols] FP16 matrix, box {box_cols columns, box_rows rows}:
+// operands 64 x 128 with a 128-byte swizzle, the output store box 32 x 32
+// with a 64-byte swizzle (the kernel's staging layout).
+bool EncodeFp16(CUtensorMap* map, const void* base, int rows, int cols, int box_cols, int box_rows,
+                CUtensorMapSwizzle swizzle) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
-  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t element_strides[2] = {1, 1};
   return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-                  element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+                  element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -134,9 +137,9 @@ extern "C" int ctb_gemm_f16_noalloc(const void* a, const void* b_t, void* c, int
 
   // Host-side descriptors (passed by value as __grid_constant__ parameters).
   ctb::tc::TmaDescriptor tma_a, tma_b, tma_out;
-  if (!EncodeFp16(reinterpret_cast<CUtensorMap*>(&tma_a), a, m, k, 128) ||
-      !EncodeFp16(reinterpret_cast<CUtensorMap*>(&tma_b), b_t, n, k, 128) ||
-      !EncodeFp16(reinterpret_cast<CUtensorMap*>(&tma_out), c, m, n, 32)) {
+  if (!EncodeFp16(reinterpret_cast<CUtensorMap*>(&tma_a), a, m, k, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !EncodeFp16(reinterpret_cast<CUtensorMap*>(&tma_b), b_t, n, k, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !EncodeFp16(reinterpret_cast<CUtensorMap*>(&tma_out), c, m, n, kChunk, 32, CU_TENSOR_MAP_SWIZZLE_64B)) {
     return Fail(error, error_len, CTB_NOALLOC_CUDA_ERROR, "cuTensorMapEncodeTiled rejected an operand");
   }
   const auto s = static_cast<cudaStream_t>(stream);
@@ -147,9 +150,9 @@ extern "C" int ctb_gemm_f16_noalloc(const void* a, const void* b_t, void* c, int
   const unsigned grid = static_cast<unsigned>(tiles < setup.sm_count ? tiles : setup.sm_count);
   __half* out = static_cast<__half*>(c);
   if (apply_gelu) {
-    ctb_gemm_gelu_f16_tp<<<grid, 320, kSmemBytes, s>>>(tma_a, tma_b, tma_out, out, m, n, k, setup.scratch, nullptr);
+    ctb_gemm_gelu_f16_tp<<<grid, kThreads, kSmemBytes, s>>>(tma_a, tma_b, tma_out, out, m, n, k, setup.scratch, nullptr);
   } else {
-    ctb_gemm_f16_tp<<<grid, 320, kSmemBytes, s>>>(tma_a, tma_b, tma_out, out, m, n, k, setup.scratch, nullptr);
+    ctb_gemm_f16_tp<<<grid, kThreads, kSmemBytes, s>>>(tma_a, tma_b, tma_out, out, m, n, k, setup.scratch, nullptr);
   }
   status = cudaGetLastError();
   if (status != cudaSuccess) return FailCuda(error, error_len, "kernel launch", status);

@@ -352,7 +352,7 @@ def _gemm_specs() -> list[KernelSpec]:
         arg("tma_a", "tensormap", "tensor_map", tensor="input", index=0, box=[64, 128], swizzle=128),
         arg("tma_b", "tensormap", "tensor_map", tensor="input", index=1, box=[64, 128], swizzle=128,
             prepack="transpose_2d"),
-        arg("tma_out", "tensormap", "tensor_map", tensor="output", index=0, box=[64, 32], swizzle=128, optional=1),
+        arg("tma_out", "tensormap", "tensor_map", tensor="output", index=0, box=[32, 32], swizzle=64, optional=1),
         arg("output", "*fp16", "output", index=0),
         arg("m", "i32", "output_dim", index=0, axis=0),
         arg("n", "i32", "output_dim", index=0, axis=1),
@@ -360,7 +360,7 @@ def _gemm_specs() -> list[KernelSpec]:
     ) + RESERVED
     tp_grid = ({"kind": "min", "args": [mul(ceil_div(out_dim(0), meta("BLOCK_M")), ceil_div(out_dim(1), meta("BLOCK_N"))),
                                         {"kind": "sm_count"}]},)
-    tp_variant = Variant("persistent_m128n256k64_2acc", num_warps=10, shared_memory_bytes=196608 + 32768 + 256 + 1024,
+    tp_variant = Variant("persistent_m128n256k64_2acc", num_warps=18, shared_memory_bytes=196608 + 32768 + 256 + 1024,
                          meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=True)
     tc = [
         KernelSpec(kernel_id="gemm.fp16.tcgen05_persistent", op_type="Gemm", version=1, source="gemm_f16_tp.cu",
