@@ -593,23 +593,32 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     int g = 0;
     int windows_issued = 0;
     bool stop = false;
+    // Window of tile L into buffer L % 2 once the gather groups have released
+    // tile L - 2's. Tile L + 1's window is issued from the middle of tile L's
+    // weight loop (block win_issue_block), so its copy lands before the gather
+    // reaches it; issued with the tile's own weights it arrived late once per
+    // tile. Waiting there for tile L - 1's release cannot stall: every copy
+    // tile L - 1 needs is already issued.
+    auto issue_window = [&](int L) -> bool {
+      const int wb = L & 1;
+      if (L >= 2 && !mbar_wait(&bars->win_empty[wb], ((L >> 1) - 1) & 1, abort, scratch, 44)) return false;
+      const Window win = window_of(blockIdx.x + static_cast<long long>(L) * gridDim.x);
+      if (win.ok) {
+        mbar_arrive_expect_tx(&bars->win_full[wb], kWinBytes);
+        tma_load_4d(windows + wb * (kWinBytes / 4), tma_xwin, &bars->win_full[wb], -4, win.ih_lo, 0, win.img);
+      } else {
+        mbar_arrive(&bars->win_full[wb]);
+      }
+      windows_issued = L + 1;
+      return true;
+    };
+    const int win_issue_block = min(2, k_blocks - 1);
     for (int local = 0; local < my_tiles && !stop; ++local) {
       const long long tile = blockIdx.x + static_cast<long long>(local) * gridDim.x;
       const int co0 = static_cast<int>(tile % co_tiles) * BN;
       int a_hw0 = 0, a_img = 0;
       const bool tile_uses_a_tma = tile_a_tma(tile, &a_hw0, &a_img);
-      if (window_shape) {
-        const int wb = local & 1;
-        if (local >= 2 && !mbar_wait(&bars->win_empty[wb], ((local >> 1) - 1) & 1, abort, scratch, 44)) break;
-        const Window win = window_of(tile);
-        if (win.ok) {
-          mbar_arrive_expect_tx(&bars->win_full[wb], kWinBytes);
-          tma_load_4d(windows + wb * (kWinBytes / 4), tma_xwin, &bars->win_full[wb], -4, win.ih_lo, 0, win.img);
-        } else {
-          mbar_arrive(&bars->win_full[wb]);
-        }
-        windows_issued = local + 1;
-      }
+      if (window_shape && local == 0 && !issue_window(0)) break;
       for (int kb = 0; kb < k_blocks; ++kb, ++g) {
         const int s = g % kStages;
         const int use = g / kStages;
@@ -636,6 +645,11 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
           } else {
             mbar_arrive(&bars->a_full[sa]);
           }
+        }
+        if (window_shape && kb == win_issue_block && local + 1 < my_tiles && !issue_window(local + 1)) {
+          stop = true;
+          ++g;  // this block's weight copies are issued: the abort drain waits for them
+          break;
         }
       }
     }
