@@ -692,7 +692,7 @@ def main() -> None:
         line = base_line(args, world)
         line.update({"value": rn["value"], "ms_per_step": rn["ms_per_step"], "roofline": rn["roofline"],
                      "clocks": rn["clocks"], "gpu_launches": rn["launches_per_step"] * args.steps,
-                     "whole_net_tflops": rn["whole_net_tflops"]})
+                     "whole_net_tflops": rn["whole_net_tflops"], "step_ms": rn["step_ms"]})
         if "e2e" in rn:
             line["e2e"] = rn["e2e"]
         if ffn is not None:
