@@ -485,6 +485,8 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     const uint32_t lane_bits = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const long long plane = static_cast<long long>(p.h) * p.w;
     const int items = my_tiles * k_blocks;  // this CTA's k blocks, in issue order
+    int px_local = -1;
+    PixelSource px_cached{x, 0, 0, false};
     // Returns false when the kernel is aborting (window wait abandoned).
     auto fetch = [&](int item, float (&v)[kBK]) -> bool {
       const int local = item / k_blocks;
@@ -532,10 +534,13 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         if (item + kGatherGroups >= last_end) mbar_arrive(&bars->win_empty[wb]);  // group's last item of the tile
         return true;
       }
-      const PixelSource px =
-          pixel_source(x, p, row < tile_rows(tile / co_tiles) ? tile_p0(tile / co_tiles) + row : total_pixels,
-                       total_pixels, pixels_per_image);
-      gather_block(px, p, cp, kdim, plane, kb, use_table ? chunk_table : nullptr, v);
+      // The pixel's source row changes once per tile: 64-bit divisions only then.
+      if (local != px_local) {
+        px_local = local;
+        px_cached = pixel_source(x, p, row < tile_rows(tile / co_tiles) ? tile_p0(tile / co_tiles) + row : total_pixels,
+                                 total_pixels, pixels_per_image);
+      }
+      gather_block(px_cached, p, cp, kdim, plane, kb, use_table ? chunk_table : nullptr, v);
       return true;
     };
     // Splits one block into hi / lo and writes it to the stage's TMEM columns.
