@@ -487,6 +487,8 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     const int items = my_tiles * k_blocks;  // this CTA's k blocks, in issue order
     int px_local = -1;
     PixelSource px_cached{x, 0, 0, false};
+    int win_local = -1, win_base = -1;
+    bool win_valid = false;
     // Returns false when the kernel is aborting (window wait abandoned).
     auto fetch = [&](int item, float (&v)[kBK]) -> bool {
       const int local = item / k_blocks;
@@ -506,15 +508,25 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
             !mbar_wait(&bars->win_full[wb], (local >> 1) & 1, abort, scratch, 43)) {
           return false;
         }
-        const Window win = window_of(tile);
-        if (win.ok) {
-          const long long mt = tile / co_tiles;
-          const bool valid = row < tile_rows(mt);
-          const long long pixel = tile_p0(mt) + row;
-          const int rem = static_cast<int>(pixel - static_cast<long long>(win.img) * pixels_per_image);
-          const int oh = rem / p.out_w;
-          const int ow = rem - oh * p.out_w;
-          const int base = (oh * p.stride_h - p.pad_h - win.ih_lo) * kWinW + ow * p.stride_w - p.pad_w + 4;
+        // The tile's window and this pixel's offset in it change once per
+        // tile; base < 0 marks a tile without a window (or a pixel past it).
+        if (local != win_local) {
+          win_local = local;
+          const Window win = window_of(tile);
+          win_base = -1;
+          if (win.ok) {
+            const long long mt = tile / co_tiles;
+            const long long pixel = tile_p0(mt) + row;
+            const int rem = static_cast<int>(pixel - static_cast<long long>(win.img) * pixels_per_image);
+            const int oh = rem / p.out_w;
+            const int ow = rem - oh * p.out_w;
+            win_base = (oh * p.stride_h - p.pad_h - win.ih_lo) * kWinW + ow * p.stride_w - p.pad_w + 4;
+            win_valid = row < tile_rows(mt);
+          }
+        }
+        if (win_base >= 0) {
+          const bool valid = win_valid;
+          const int base = win_base;
           const float* win_buf = windows + wb * (kWinBytes / 4);
 #pragma unroll
           for (int j = 0; j < kBK / 4; ++j) {
