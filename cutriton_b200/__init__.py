@@ -271,6 +271,10 @@ class ExecutionContext:
     def __init__(self, handle: ctypes.c_void_p, engine: Engine) -> None:
         self._h = handle
         self._engine = engine  # keeps plan inspection alive; the C++ context does not need it
+        # Tensors bound through bind_tensor, by name: the context holds only
+        # their addresses, so it keeps them alive until rebound or destroyed
+        # (a freed tensor's memory would be handed to the next allocation).
+        self._bound: dict[str, object] = {}
 
     def __del__(self) -> None:
         if getattr(self, "_h", None) and _lib is not None:
@@ -281,15 +285,21 @@ class ExecutionContext:
             self._h = None
 
     def bind_input(self, name: str, device_ptr: int, nbytes: int) -> None:
+        """Binds device memory by address; the caller keeps it alive."""
         _check(library().ctb_context_bind_input(self._h, name.encode(), _P(device_ptr), nbytes))
+        self._bound.pop(name, None)
 
     def bind_output(self, name: str, device_ptr: int, nbytes: int) -> None:
+        """Binds device memory by address; the caller keeps it alive."""
         _check(library().ctb_context_bind_output(self._h, name.encode(), _P(device_ptr), nbytes))
+        self._bound.pop(name, None)
 
     def bind_tensor(self, name: str, tensor, output: bool = False) -> None:
-        """Binds a CUDA torch tensor (contiguous) by its data pointer."""
+        """Binds a CUDA torch tensor (contiguous) by its data pointer and keeps
+        a reference to it for as long as it is bound."""
         nbytes = tensor.numel() * tensor.element_size()
         (self.bind_output if output else self.bind_input)(name, tensor.data_ptr(), nbytes)
+        self._bound[name] = tensor
 
     def select_profile(self, name: str) -> None:
         _check(library().ctb_context_select_profile(self._h, name.encode()))
