@@ -7,16 +7,17 @@
 // K-major and staged by TMA in the 128-byte-swizzled layout the UMMA
 // descriptors read.
 //
-// One CTA per SM walks the 128 x BN output tiles (BN = 256, or 128 when that
-// saves enough waves on a small problem) in a static round-robin, N fastest so
-// co-running CTAs share the A tile in L2. Roles (18 warps):
+// One CTA per SM walks the 128 x BN output tiles (BN = 256, 192 or 128,
+// whichever gives the fewest estimated waves x tile cost) in a static
+// round-robin, N fastest so co-running CTAs share the A tile in L2. Roles
+// (18 warps):
 //   warp 0 lane 0 — TMA producer: A (128 x 64) and B (BN x 64) per k block
 //       through a STAGES-deep shared-memory ring (full / empty barriers);
 //   warp 1 lane 0 — UMMA issuer: 4 x (128 x BN x 16) per k block into one of
 //       two TMEM accumulators (2 x BN columns), so the epilogue of one tile
 //       overlaps the MMAs of the next;
 //   warps 2-17 — epilogue, four warps per TMEM lane quarter (warp % 4 = 32
-//       rows), each taking a quarter of the columns, 32 at a time -> GELU ->
+//       rows), taking the quarter's 32-column chunks in turn -> GELU ->
 //       FP16 -> a 32 x 32 staging box in shared memory (64-byte swizzle,
 //       conflict-free 16-byte writes) -> TMA tensor store; each warp hands its
 //       columns of the accumulator back as soon as they are in registers.
@@ -48,11 +49,18 @@ constexpr int kMaxStages = 6;
 
 template <int BN>
 struct Config {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
-  static constexpr uint32_t kTileB = BN * kBK * 2;
+  // B arrives in 128-row boxes: a 192-wide tile loads two (the last 64 rows
+  // unused), so its stage is as large as a 256-wide one's.
+  static constexpr int kBoxesB = (BN + kBoxRowsB - 1) / kBoxRowsB;
+  static constexpr int kStages = BN == 128 ? 6 : 4;
+  static constexpr uint32_t kTileB = kBoxesB * kBoxRowsB * kBK * 2;
   static constexpr uint32_t kStageBytes = kTileA + kTileB;
   static_assert(kStages * kStageBytes <= kRingBytes, "shared memory ring");
   static_assert(2 * BN <= 512, "TMEM accumulators");
+  // Two accumulators of BN columns; allocations are powers of two.
+  static constexpr uint32_t kTmemCols = (2 * BN) & (2 * BN - 1) ? 512 : 2 * BN;
+  static constexpr int kChunks = BN / kChunk;  // 32-column epilogue chunks per lane quarter
+  static_assert(BN % kChunk == 0 && kChunks >= kEpilogueWarps / 4, "every epilogue warp takes a chunk");
 };
 
 struct __align__(8) Barriers {
@@ -111,7 +119,7 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
     tma_prefetch(tma_b);
     if (tma_epilogue) tma_prefetch(tma_out);
   }
-  if (warp == 0) tmem_alloc(&bars->tmem_base, 2 * BN);
+  if (warp == 0) tmem_alloc(&bars->tmem_base, C::kTmemCols);
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
@@ -137,7 +145,7 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
         mbar_arrive_expect_tx(&bars->full[s], C::kStageBytes);
         tma_load_2d(tile_a(s), tma_a, &bars->full[s], kb * kBK, m0);
 #pragma unroll
-        for (int b = 0; b < BN / static_cast<int>(kBoxRowsB); ++b) {
+        for (int b = 0; b < C::kBoxesB; ++b) {
           tma_load_2d(tile_b(s) + b * kBoxRowsB * 128, tma_b, &bars->full[s], kb * kBK, n0 + b * kBoxRowsB);
         }
       }
@@ -187,11 +195,12 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
       mbar_wait(&bars->drain, 0, &never, scratch, 54);
     }
   } else if (warp >= kEpilogueWarp0) {
-    // ---- epilogue: rows quarter*32 + lane, columns [c_begin, c_begin + BN/4) ----
-    constexpr int kSpan = BN / (kEpilogueWarps / 4);
+    // ---- epilogue: rows quarter*32 + lane; the quarter's 32-column chunks
+    // are dealt round-robin to its four warps (chunk ci to warp ci % 4) ----
     constexpr int kPacks = kChunk / 8;
+    constexpr int kWarpsPerQuarter = kEpilogueWarps / 4;
     const int quarter = warp & 3;
-    const int c_begin = ((warp - kEpilogueWarp0) / 4) * kSpan;
+    const int wq = (warp - kEpilogueWarp0) / 4;  // this warp's rank within its quarter
     uint8_t* box = staging + (warp - kEpilogueWarp0) * kStageBoxBytes;
     bool box_used = false;
     for (int local = 0; local < my_tiles; ++local) {
@@ -206,10 +215,11 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
       const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
       const int row = m0 + quarter * 32 + lane;
 #pragma unroll 1
-      for (int c = c_begin; c < c_begin + kSpan; c += kChunk) {
+      for (int ci = wq; ci < C::kChunks; ci += kWarpsPerQuarter) {
+        const int c = ci * kChunk;
         uint32_t v[kChunk];
         tmem_load_32x32(taddr + c, v);
-        if (c + kChunk == c_begin + kSpan) {
+        if (ci + kWarpsPerQuarter >= C::kChunks) {
           // This warp's columns of the accumulator are in registers: hand them back.
           tc_fence_before_sync();
           __syncwarp();
@@ -230,7 +240,9 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
             h[j] = __floats2half2_rn(a, b);
           }
         }
-        if (tma_epilogue) {
+        if (n0 + c >= n) {
+          // Columns past N (a partial last tile): nothing to store.
+        } else if (tma_epilogue) {
           if (box_used) {
             // The previous store from this box has read it out.
             if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -264,7 +276,7 @@ __device__ __forceinline__ void gemm_tp(uint8_t* smem, const TmaDescriptor* tma_
   tc_fence_after_sync();
   if (warp == 0) {
     __syncwarp();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 
@@ -276,14 +288,19 @@ __device__ __forceinline__ void gemm_tp_dispatch(const TmaDescriptor* tma_a, con
   // 1024-byte alignment for the 128-byte swizzle atoms.
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const long long m_tiles = (m + kBM - 1) / kBM;
-  // Waves of 256- vs 128-wide tiles; a 128-wide tile costs ~0.69 of a
-  // 256-wide one at steady state (measured), so 128 wins only when it saves
-  // enough waves (small problems).
+  // Estimated time = waves x per-tile cost, relative to a 256-wide tile (100):
+  // a 128-wide tile costs ~69 at steady state (measured), a 192-wide one ~80
+  // (three quarters of the MMAs, two B boxes). 192 wins where 256-wide tiles
+  // leave SMs idle, e.g. N = 768 at M = 4096: 96 tiles on 148 SMs.
   const long long g = gridDim.x;
   const long long w256 = (m_tiles * ((n + 255) / 256) + g - 1) / g;
+  const long long w192 = (m_tiles * ((n + 191) / 192) + g - 1) / g;
   const long long w128 = (m_tiles * ((n + 127) / 128) + g - 1) / g;
-  if (100 * w256 <= 69 * w128) {
+  const long long t256 = 100 * w256, t192 = 80 * w192, t128 = 69 * w128;
+  if (t256 <= t192 && t256 <= t128) {
     gemm_tp<kGelu, 256>(smem, tma_a, tma_b, tma_out, out, m, n, k, scratch);
+  } else if (t192 <= t128) {
+    gemm_tp<kGelu, 192>(smem, tma_a, tma_b, tma_out, out, m, n, k, scratch);
   } else {
     gemm_tp<kGelu, 128>(smem, tma_a, tma_b, tma_out, out, m, n, k, scratch);
   }

@@ -184,8 +184,9 @@ def test_gemm_f32(cuda, mnk):
 
 
 @pytest.mark.parametrize("mnk", [(256, 3072, 768), (17, 512, 128), (128, 768, 3072), (33, 200, 72),
-                                 # persistent kernel: >1 tile per CTA with 128-wide tiles, and 256-wide tiles
-                                 (1280, 2560, 64), (2048, 4864, 128)])
+                                 # persistent kernel, several tiles per CTA: 192-wide tiles with a partial
+                                 # last tile (N not a multiple of 192), 192-wide at N = 768, 256-wide tiles
+                                 (1280, 2560, 64), (2048, 4864, 128), (4096, 768, 512), (4096, 3072, 256)])
 @pytest.mark.parametrize("op", ["Gemm", "GemmGelu"])
 def test_gemm_f16(cuda, mnk, op):
     m, n, k = mnk
