@@ -150,3 +150,47 @@ def test_pack_entries_are_cubins_for_sm100():
         op_defaults.setdefault((k["op_type"], k["dtype"]), []).append(k["default"])
     for key, flags in op_defaults.items():
         assert sum(flags) == 1, key
+
+
+def _kernel_constant(source: str, name: str) -> int:
+    import re
+
+    match = re.search(rf"constexpr int {name} = (\d+);", source)
+    assert match, f"{name} not found"
+    return int(match.group(1))
+
+
+def test_launch_shapes_match_the_kernels():
+    """The launcher takes block size, shared memory and tensor-map boxes from
+    the pack; each must agree with what the kernel was compiled to expect."""
+    from cutriton_b200 import kernel_specs
+    from cutriton_b200.kernel_sdk import _variant_arguments
+
+    kernels = Path(kernel_specs.__file__).resolve().parent / "csrc" / "kernels"
+    gemm = (kernels / "gemm_f16_tp.cu").read_text()
+    epilogue_warps = _kernel_constant(gemm, "kEpilogueWarps")
+    chunk = _kernel_constant(gemm, "kChunk")
+    checked = set()
+    for spec in kernel_specs.all_specs():
+        for variant in spec.variants:
+            args = {a["name"]: a["source"] for a in _variant_arguments(spec, variant)}
+            if spec.source == "gemm_f16_tp.cu":
+                # producer + issuer + epilogue warps; 32 x chunk FP16 store box, swizzle = its row bytes
+                assert variant.num_warps == 2 + epilogue_warps, spec.kernel_id
+                assert args["tma_out"]["box"] == [chunk, 32], spec.kernel_id
+                assert args["tma_out"]["swizzle"] == 2 * chunk, spec.kernel_id
+                checked.add(spec.source)
+            if spec.source == "conv_tm.cu":
+                d = variant.defines
+                warps = 2 + int(d["CTB_TM_EPI_WARPS"]) + 4 * int(d["CTB_TM_GATHER_GROUPS"])
+                assert variant.num_warps == warps, (spec.kernel_id, variant.variant_id)
+                # weight stages + barriers + chunk table + staging ring + activation ring + windows + alignment
+                stages = max(int(d["CTB_TM_STAGES_N128"]) * 32768, int(d["CTB_TM_STAGES_N64"]) * 16384)
+                need = stages + 512 + 1024 + int(d["CTB_TM_SLOTS"]) * 16384 + 1024
+                if d["CTB_TM_A_TMA"] == "1":
+                    need += 4 * 16384
+                if d.get("CTB_TM_WINDOW") == "1":
+                    need += 2 * 232 * 11 * 4 * 4
+                assert need <= variant.shared_memory_bytes <= 232448, (spec.kernel_id, variant.variant_id)
+                checked.add(spec.source)
+    assert checked == {"gemm_f16_tp.cu", "conv_tm.cu"}
