@@ -12,7 +12,7 @@ the committed .npz files).
   336-393 (tokens 17, hidden 128, intermediate 512; GEMM, exact GELU,
   residual add, LayerNorm), restated in numpy (float64 statistics).
 
-Usage: python tests/golden/make_golden.py [--reference /path/to/checkout]
+Usage: python tests/golden/make_golden.py --reference /path/to/checkout
 """
 
 from __future__ import annotations
@@ -78,7 +78,8 @@ def ffn17_known_answer() -> None:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference", type=Path, required=True,
+                        help="checkout of the reference project (read only)")
     args = parser.parse_args()
     stem_known_answer()
     ffn17_known_answer()
