@@ -130,7 +130,9 @@ size_t ctb_engine_workspace_bytes(ctb_engine engine);
 int ctb_context_create(ctb_engine engine, ctb_context* out);
 void ctb_context_destroy(ctb_context context);
 /* BindInput/BindOutput of device memory on the plan's device. `nbytes` is
- * the usable size of the allocation at `device_ptr`. */
+ * the usable size of the allocation at `device_ptr`. The context keeps only
+ * the address: the caller keeps the memory alive until it rebinds the name or
+ * destroys the context. */
 int ctb_context_bind_input(ctb_context context, const char* name, void* device_ptr, size_t nbytes);
 int ctb_context_bind_output(ctb_context context, const char* name, void* device_ptr, size_t nbytes);
 int ctb_context_select_profile(ctb_context context, const char* profile);
@@ -142,8 +144,8 @@ int ctb_context_run(ctb_context context);
 /* `stream` is a CUstream / cudaStream_t on the plan's device, or NULL. */
 int ctb_context_run_async(ctb_context context, void* stream);
 int ctb_context_synchronize(ctb_context context);
-/* Profiler events of the last synchronized run: count, then per event the
- * duration (ms). Names via ctb_context_profile_event_name. */
+/* Profiler events of the last synchronized run: count, then per event its
+ * name (written into `name`) and duration (ms). */
 int ctb_context_profile_event_count(ctb_context context);
 int ctb_context_profile_event(ctb_context context, int index, char* name, size_t name_len,
                               double* duration_ms);
@@ -155,7 +157,9 @@ int ctb_context_selected_candidate(ctb_context context, int op);
  * SelectCandidate; overrides the default and the tuner). */
 int ctb_context_select_candidate(ctb_context context, int op, int candidate);
 
-/* End-to-end call with host buffers: copies each input from host memory to
+/* Extensions without a counterpart in the reference, whose harnesses copy
+ * host buffers themselves around RunAsync.
+ * End-to-end call with host buffers: copies each input from host memory to
  * the bound device buffer, runs, and copies each output back, all ordered on
  * `stream` (NULL: the context stream); returns after the copies complete.
  * Inputs/outputs must already be bound (their device buffers are reused). */
