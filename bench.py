@@ -661,8 +661,9 @@ def main() -> None:
         dt = time.perf_counter() - t0
         value = batch * args.steps / dt
         sample = f"PyTorch eager FP32 ResNet-50 on {threads} host threads, batch {batch} per step"
-        line.update({"value": value, "ms_per_step": dt / args.steps * 1e3, "n_gpus": 0,
-                     "config": {**line["config"], "batch_per_step": batch},
+        line.update({"value": value, "ms_per_step": dt / args.steps * 1e3,
+                     "config": {**line["config"], "batch_per_step": batch,
+                                "compute": "host CPU on rank 0 (no GPU used)"},
                      "cpu_baseline": {"value": value, "unit": "img/s", "cores": threads, "kind": "port",
                                       "sample": sample},
                      "e2e": {"value": value, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})

@@ -44,3 +44,26 @@ def test_peaks_come_from_the_measured_file_when_present():
     for key in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained"):
         assert peaks[key] > 0
     assert kind == ("measured" if bench.PEAKS_FILE.exists() else "fallback")
+
+
+def test_reference_arm_under_torchrun_prints_one_line():
+    """`bench.py --impl reference` launched like the GPU arm at N=2: rank 0
+    times the CPU path and prints one JSON line, the other rank exits 0."""
+    import json
+    import socket
+    import subprocess
+    import sys
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), str(bench.REPO / "bench.py"),
+           "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "1"]
+    done = subprocess.run(cmd, capture_output=True, text=True, timeout=600, cwd=bench.REPO)
+    assert done.returncode == 0, done.stderr[-2000:]
+    lines = [l for l in done.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["value"] > 0
+    assert line["cpu_baseline"]["value"] == line["value"] and line["e2e"]["h2d_bytes_per_step"] == 0
