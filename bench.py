@@ -11,9 +11,12 @@ stream, max over ranks. Inputs (154 MB per step) are larger than L2.
 The line also reports: the end-to-end rate through the C ABI with host
 buffers (pinned H2D of the step's images + D2H of the logits inside the
 timed region), the roofline of the dominant kernel family (the FP32
-convolutions), the FFN FP16 block (config 1: M=4096, H=768, I=3072), the
-PyTorch-eager CPU baseline on a bounded sample, and SM clocks sampled during
-the timed region.
+convolutions), the FFN FP16 block at config 1 (M=4096, H=768, I=3072, per
+rank) and config 4 (H=1024, I=4096, global M=65536 split over the ranks),
+SM clocks sampled during the timed region, and — from the CPU leg on rank 0,
+after all GPU timing — the PyTorch-eager CPU baseline on a bounded sample and
+a parity check of the bench's own GPU outputs against the CPU results
+(sampled bs256 logits; the whole config-1 FFN output).
 
 ``--impl reference`` times the reference's CPU comparison path (the PyTorch
 eager ResNet-50 of the reference's benchmarks/resnet50_compare.py, restated
@@ -110,26 +113,136 @@ def _ffn_case():
     return e, ctx, (x, y)
 
 
-# Single-kernel cases for ncu captures: inputs + outputs above L2 (126 MB), a few
-# hundred MB on the device.
+def _single_op_case(op: str, shapes: list[tuple[str, list[int]]], out_shape: list[int], dtype: str = "float32",
+                    constants: dict | None = None, **attrs):
+    """One node `op` over inputs of `shapes` through the engine; returns (engine, ctx, tensors)."""
+    import torch
+    import cutriton_b200 as ct
+
+    np_dtype = np.float16 if dtype == "float16" else np.float32
+    layout = "NCHW" if len(out_shape) == 4 else ""
+    m = ct.Model()
+    names = []
+    for name, shape in shapes:
+        m.add_input(name, shape, dtype=np_dtype, layout=layout)
+        names.append(name)
+    for name, value in (constants or {}).items():
+        m.add_constant(name, value, layout="")
+        names.append(name)
+    m.add_node("op", op, names, ["y"], **attrs)
+    m.add_output("y")
+    e = ct.build_engine(m, enable_cuda_graph=False, tuning_mode=ct.TUNING_DISABLED)
+    ctx = e.create_context()
+    tdtype = getattr(torch, dtype)
+    keep = []
+    for name, shape in shapes:
+        keep.append(torch.randn(*shape, device="cuda").to(tdtype))
+        ctx.bind_tensor(name, keep[-1])
+    keep.append(torch.empty(*out_shape, device="cuda", dtype=tdtype))
+    ctx.bind_tensor("y", keep[-1], output=True)
+    return e, ctx, keep
+
+
+def _skip_ln_case(rows: list[int]):
+    import torch
+    import cutriton_b200 as ct
+
+    m = ct.Model()
+    m.add_input("x", rows, dtype=np.float16, layout="")
+    m.add_input("r", rows, dtype=np.float16, layout="")
+    m.add_constant("g", np.ones(rows[1], np.float16), layout="")
+    m.add_constant("b", np.zeros(rows[1], np.float16), layout="")
+    m.add_node("add", "Add", ["x", "r"], ["s"])
+    m.add_node("ln", "LayerNormalization", ["s", "g", "b"], ["y"], axis=-1, epsilon=1e-5)
+    m.add_output("y")
+    e = ct.build_engine(m, enable_cuda_graph=False, tuning_mode=ct.TUNING_DISABLED)
+    ctx = e.create_context()
+    keep = [torch.randn(*rows, device="cuda").half() for _ in range(3)]
+    ctx.bind_tensor("x", keep[0])
+    ctx.bind_tensor("r", keep[1])
+    ctx.bind_tensor("y", keep[2], output=True)
+    return e, ctx, keep
+
+
+def _bandwidth_cases():
+    """Every bandwidth-bound kernel of the pack at a size above L2 (126 MB)
+    and a few hundred MB on the device, plus the FC GEMM at bs256."""
+    nchw = [64, 256, 56, 56]  # 205.5 MB per FP32 tensor
+    rows = [65536, 1024]      # 134 MB per FP16 tensor
+    bn = {n: np.ones(256, np.float32) for n in ("s", "b", "m", "v")}
+    ln = {"g": np.ones(1024, np.float16), "b": np.zeros(1024, np.float16)}
+    return [
+        ("max_pool_3x3s2_f32_64x64x112x112", lambda: _single_op_case(
+            "MaxPool", [("x", [64, 64, 112, 112])], [64, 64, 56, 56], kernel_shape=[3, 3], strides=[2, 2],
+            pads=[1, 1, 1, 1], dilations=[1, 1])),
+        ("global_average_pool_f32_512x2048x7x7", lambda: _single_op_case(
+            "GlobalAveragePool", [("x", [512, 2048, 7, 7])], [512, 2048, 1, 1])),
+        ("add_relu_f32_64x256x56x56", lambda: _single_op_case("AddRelu", [("a", nchw), ("b", nchw)], nchw)),
+        ("add_f32_64x256x56x56", lambda: _single_op_case("Add", [("a", nchw), ("b", nchw)], nchw)),
+        ("relu_f32_64x256x56x56", lambda: _single_op_case("Relu", [("a", nchw)], nchw)),
+        ("batch_norm_f32_64x256x56x56", lambda: _single_op_case(
+            "BatchNormalization", [("x", nchw)], nchw, constants=bn, epsilon=1e-5)),
+        ("gelu_f16_65536x1024", lambda: _single_op_case("Gelu", [("x", rows)], rows, dtype="float16")),
+        ("add_f16_65536x1024", lambda: _single_op_case("Add", [("a", rows), ("b", rows)], rows, dtype="float16")),
+        ("layer_norm_f16_65536x1024", lambda: _single_op_case(
+            "LayerNormalization", [("x", rows)], rows, dtype="float16", constants=ln, axis=-1, epsilon=1e-5)),
+        ("skip_layer_norm_f16_65536x1024", lambda: _skip_ln_case(rows)),
+        ("fc_gemm_f32_256x2048x1000", lambda: _single_op_case(
+            "Gemm", [("a", [256, 2048])], [256, 1000], constants={"w": np.full((2048, 1000), 0.01, np.float32)})),
+    ]
+
+
+def _resnet_case(batch: int):
+    import torch
+    import cutriton_b200 as ct
+    from cutriton_b200 import workloads
+
+    model = workloads.build_resnet50(workloads.resnet50_weights("baseline", seed=0), batch=batch)
+    e = ct.build_engine(model, enable_cuda_graph=False, enable_residual_fusion=True, tuning_mode=ct.TUNING_DISABLED)
+    ctx = e.create_context()
+    x = torch.from_numpy(workloads.resnet50_input(batch, seed=0)).cuda()
+    y = torch.empty(batch, 1000, device="cuda")
+    ctx.bind_tensor("input", x)
+    ctx.bind_tensor("output", y, output=True)
+    return e, ctx, (x, y)
+
+
+# Cases for ncu captures: inputs + outputs above L2 (126 MB), at most a few GB
+# on the device. A single-kernel case runs three times; "bandwidth_ops" runs
+# each of its graphs once, one after the other (built, run, freed);
+# "resnet50_bs32" / "resnet50_bs64" run the whole network once each (per-layer
+# DRAM traffic at two batch sizes, extrapolated to bs256 by a fit linear in
+# the batch).
 PROFILE_CASES = {
     "conv3x3_128ch_28x28_bs256": lambda: _conv_case(256, 128, 28, 128, 3, 1, 1),
+    "conv3x3_64ch_56x56_bs64": lambda: _conv_case(64, 64, 56, 64, 3, 1, 1),
     "conv1x1_256to64_56x56_bs64": lambda: _conv_case(64, 256, 56, 64, 1, 1, 0),
     "conv1x1_64to256_add_56x56_bs64": lambda: _conv_case(64, 64, 56, 256, 1, 1, 0, residual=True),
     "stem7x7_bs64": lambda: _conv_case(64, 3, 224, 64, 7, 2, 3),
     "ffn_4096x768x3072": _ffn_case,
+    "bandwidth_ops": None,
+    "resnet50_bs32": lambda: _resnet_case(32),
+    "resnet50_bs64": lambda: _resnet_case(64),
 }
 
 
 def run_profile_case(name: str) -> None:
     import torch
 
+    if name == "bandwidth_ops":
+        for case, make in _bandwidth_cases():
+            keep = make()
+            keep[1].run()
+            torch.cuda.synchronize()
+            print(json.dumps({"profile_case": case, "runs": 1}), flush=True)
+            del keep
+        return
     keep = PROFILE_CASES[name]()
-    ctx = keep[1]
-    for _ in range(3):
-        ctx.run()
+    runs = 1 if name.startswith("resnet50_") else 3
+    for _ in range(runs):
+        keep[1].run()
     torch.cuda.synchronize()
-    print(json.dumps({"profile_case": name, "runs": 3}), flush=True)
+    print(json.dumps({"profile_case": name, "runs": runs}), flush=True)
 
 
 def conv_shapes() -> list[tuple[int, int, int, int, int, int]]:
@@ -154,8 +267,9 @@ def conv_shapes() -> list[tuple[int, int, int, int, int, int]]:
     return shapes
 
 
-def time_context(ctx, stream, steps: int, warmup: int) -> float:
-    """Median ms of `steps` RunAsync calls timed with CUDA events on `stream`."""
+def time_context(ctx, stream, steps: int, warmup: int, all_times: bool = False):
+    """Median ms of `steps` RunAsync calls timed with CUDA events on `stream`
+    (every step's ms with `all_times`)."""
     import torch
 
     for _ in range(max(3, warmup)):
@@ -170,7 +284,7 @@ def time_context(ctx, stream, steps: int, warmup: int) -> float:
         ctx.synchronize()
         b.synchronize()
         times.append(a.elapsed_time(b))
-    return float(np.median(times))
+    return times if all_times else float(np.median(times))
 
 
 def run_config2(args, tuning: str = "TuneOnMiss") -> dict:
@@ -237,7 +351,7 @@ def run_config3(args, peaks) -> dict:
             "layers": rows}
 
 
-def run_config4(args, world, rank, local) -> dict:
+def run_config4(args, world, rank, local, peaks, peak_kind) -> dict:
     """Config 4: FFN H=1024, I=4096, global M=65536 split over the ranks (no collective)."""
     import torch
     import cutriton_b200 as ct
@@ -253,11 +367,16 @@ def run_config4(args, world, rank, local) -> dict:
     y = torch.empty(m_rank, h, dtype=torch.float16, device=f"cuda:{local}")
     ctx.bind_tensor("x", x)
     ctx.bind_tensor("output", y, output=True)
-    ms = max_over_ranks(time_context(ctx, torch.cuda.Stream(local), args.steps, args.warmup), world)
+    times = time_context(ctx, torch.cuda.Stream(local), args.steps, args.warmup, all_times=True)
+    ms = max_over_ranks(float(np.median(times)), world)
+    p95 = max_over_ranks(float(np.percentile(times, 95)), world)
     flops = 4.0 * h * i * global_m
+    tflops = flops / ms / 1e9
     return {"metric": "FFN FP16 tokens/s (config 4: H=1024, I=4096, global M=65536)", "unit": "tokens/s",
-            "value": global_m / ms * 1e3, "ms_per_step": ms, "tflops": flops / ms / 1e9, "n_gpus": world,
-            "scaling": "strong", "higher_is_better": True}
+            "value": global_m / ms * 1e3, "ms_per_step": ms, "ms_p95": p95, "tflops": tflops,
+            "tflops_per_gpu": tflops / world, "roofline": ffn_roofline(tflops / world, peaks, peak_kind),
+            "rows_per_gpu": m_rank, "n_gpus": world, "scaling": "strong", "higher_is_better": True,
+            "l2": "inputs larger than L2 at 1 GPU (M=65536: 128 MB in, 512 MB intermediate)"}
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -276,7 +395,15 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index: int):
-        self.device_index = device_index
+        # nvidia-smi numbers GPUs its own way (it ignores CUDA_VISIBLE_DEVICES),
+        # so the timed GPU is named by its UUID rather than the CUDA ordinal.
+        self.device_index = str(device_index)
+        try:
+            import torch
+
+            self.device_index = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+        except Exception:  # noqa: BLE001 - keep the ordinal when the UUID is unavailable
+            pass
         self.proc = None
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"ctb_clocks_{os.getpid()}.csv"
 
@@ -284,7 +411,7 @@ class ClockSampler:
         try:
             self.out = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.device_index), "-lms", "100"], stdout=self.out,
+                                          "-i", self.device_index, "-lms", "100"], stdout=self.out,
                                          stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
@@ -321,7 +448,7 @@ class ClockSampler:
                     reasons.add(name)
         self.path.unlink(missing_ok=True)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(sm_max) if sm_max else None,
-                "samples": len(rows), "reasons": sorted(reasons)}
+                "samples": len(rows), "reasons": sorted(reasons), "gpu": self.device_index}
 
 
 def dist_setup(args):
@@ -455,6 +582,7 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
     step_ms = [marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)]
     clock_summary = clocks.summary()
+    logits = y.cpu().numpy()  # after the timed region: the parity check's input
 
     # Per-op conv times (engine profiler: CUDA events around each op).
     prof_engine = ct.build_engine(model, device_id=local, enable_cuda_graph=True, enable_profiling=True,
@@ -480,8 +608,11 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
     achieved_tflops = work["conv_flops"] / (conv_ms_avg / 1e3) / 1e12
     # FP32 convolutions run as 3xTF32 on the tensor cores: 3 TF32 MMAs (TF32
     # = half the BF16 rate) per FP32 multiply-add, so the FP32-equivalent
-    # ceiling is bf16_tflops / 6 of the measured BF16 peak.
-    peak_tflops = peaks["bf16_tflops_sustained"] / 6.0
+    # ceiling is bf16_tflops / 6 of the measured BF16 peak. Each conv launch
+    # lasts 0.1-1 ms at full clock, so the burst figure is the basis; the
+    # sustained (power-capped, seconds-long) one is reported beside it.
+    peak_tflops = peaks["bf16_tflops"] / 6.0
+    peak_sustained = peaks["bf16_tflops_sustained"] / 6.0
     result = {
         "value": value, "ms_per_step": ms_per_step, "launches_per_step": launches, "clocks": clock_summary,
         "step_ms": {"median": float(np.median(step_ms)), "p95": float(np.percentile(step_ms, 95)),
@@ -490,20 +621,22 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
             "bound": "tensor", "kernel": "FP32 convolution family (all conv ops of one step)",
             "achieved": achieved_tflops, "peak": peak_tflops, "unit": "TFLOP/s",
             "frac": achieved_tflops / peak_tflops,
+            "frac_sustained_basis": achieved_tflops / peak_sustained,
             # For transparency: the same FLOPs against a plain (1xTF32) basis,
             # half the measured BF16 rate; 3xTF32 issues three MMAs per MAC.
-            "frac_vs_plain_tf32": achieved_tflops / (peaks["bf16_tflops_sustained"] / 2.0),
-            "peak_basis": f"{peak_kind} bf16_tflops_sustained {peaks['bf16_tflops_sustained']} / 6 (3xTF32 FP32-equivalent)",
+            "frac_vs_plain_tf32": achieved_tflops / (peaks["bf16_tflops"] / 2.0),
+            "peak_basis": f"{peak_kind} bf16_tflops (burst) {peaks['bf16_tflops']} / 6 (3xTF32 FP32-equivalent); "
+                          f"frac_sustained_basis uses bf16_tflops_sustained {peaks['bf16_tflops_sustained']} / 6",
             "conv_ms_per_step": conv_ms_avg, "algorithmic_gflop_per_step": work["conv_flops"] / 1e9,
             "hbm_frac_at_min_bytes": (work["conv_bytes"] / (conv_ms_avg / 1e3) / 1e9) / peaks["hbm_gbs"],
-            # DRAM bytes (read + write) of the 53 conv launches of one bs256 step,
-            # from the one-pass ncu capture recorded in
-            # profiles/launch_list_bench_resnet50_bs256_ffn.md (not measured live).
+            # DRAM bytes (read + write) of the 53 conv launches of one bs256 step
+            # from an ncu capture (not measured live).
             "traffic": CONV_DRAM_BYTES_PER_STEP_BS256 * batch / 256,
             "traffic_unit": "bytes per step (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
             "min_bytes": work["conv_bytes"],
         },
         "whole_net_tflops": work["total_flops"] / (ms_per_step / 1e3) / 1e12,
+        "images": x_host, "logits": logits,
     }
 
     if not args.no_e2e:
@@ -555,12 +688,14 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
                          "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(host_outs[0].nbytes),
                          "steps": steps,
                          "path": "ctb_context_run_host_async (C ABI): two contexts on two streams, pinned host buffers",
+                         "h2d_gbs_per_rank": x_host.nbytes * steps / (e_ms / 1e3) / 1e9,
+                         "h2d_gbs_all_ranks": world * x_host.nbytes * steps / (e_ms / 1e3) / 1e9,
                          "serial_value": world * batch * steps / (serial_ms / 1e3),
                          "serial_path": "ctb_context_run_host (C ABI), one context, waits every step"}
     return result
 
 
-def run_ffn(args, world, rank, local) -> dict:
+def run_ffn(args, world, rank, local, peaks, peak_kind) -> dict:
     import torch
 
     import cutriton_b200 as ct
@@ -594,13 +729,57 @@ def run_ffn(args, world, rank, local) -> dict:
             ctx.synchronize()
             times.append(s.elapsed_time(e))
     med = max_over_ranks(float(np.median(times)), world)
+    p95 = max_over_ranks(float(np.percentile(times, 95)), world)
     flops = 4.0 * t * h * i
+    tflops = flops / (med / 1e3) / 1e12
     return {"metric": "FFN FP16 tokens/s (M=4096, H=768, I=3072)", "value": world * t / (med / 1e3),
-            "unit": "tokens/s", "ms_per_step": med, "tflops": flops / (med / 1e3) / 1e12,
-            "l2": "flushed (256 MB write) before every timed step"}
+            "unit": "tokens/s", "ms_per_step": med, "ms_p95": p95, "tflops": tflops,
+            "roofline": ffn_roofline(tflops, peaks, peak_kind),
+            "scaling": "weak (config 1 per rank)", "l2": "flushed (256 MB write) before every timed step",
+            "input": x.cpu().numpy(), "output": y.cpu().numpy(), "weights": w}
 
 
-def cpu_baseline(threads: int | None = None, batch: int = 8, steps: int = 2) -> dict:
+def ffn_roofline(tflops: float, peaks: dict, peak_kind: str) -> dict:
+    """FFN block (GemmGelu + Gemm + SkipLayerNorm) against the FP16 tensor
+    peak: 4*H*I FLOPs per token; the kernels run well under a millisecond at
+    full clock, so the burst BF16 figure (= FP16 rate) is the basis."""
+    return {"bound": "tensor", "kernel": "FFN block: ctb_gemm_gelu_f16_tp + ctb_gemm_f16_tp + ctb_skip_layer_norm_f16",
+            "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": tflops / peaks["bf16_tflops"], "peak_basis": f"{peak_kind} bf16_tflops (burst)"}
+
+
+def host_cpu() -> dict:
+    """Model name and core count of the host CPU (lscpu), recorded with the CPU legs."""
+    info = {"logical_cpus": os.cpu_count()}
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for row in out.splitlines():
+            key, _, value = row.partition(":")
+            if key.strip() in ("Model name", "Socket(s)", "Core(s) per socket", "Thread(s) per core"):
+                info[key.strip().lower().replace("(s)", "s").replace(" ", "_")] = value.strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+    return info
+
+
+def resnet_parity_sample(batch: int) -> np.ndarray:
+    """Images of the bs256 step whose logits are checked: the first and last
+    eight (first and last pixel tiles of every layer) and the three around
+    image 128 (tiles that straddle two images)."""
+    picked = set(range(min(8, batch))) | set(range(max(0, batch - 8), batch))
+    picked.update(i for i in (127, 128, 129) if i < batch)
+    return np.array(sorted(picked), dtype=np.int64)
+
+
+def cpu_resnet(steps: int | None, batch: int, seconds: float | None = None, threads: int | None = None,
+               images: np.ndarray | None = None) -> dict:
+    """The reference's CPU comparison path for ResNet-50 (PyTorch eager FP32,
+    benchmarks/resnet50_compare.py:118-141, restated in oracle/torch_ref.py)
+    on all host threads: one untimed warm-up step, then `steps` timed steps of
+    `batch` images (or as many as fit in `seconds`, at least two). `images`
+    replaces the seeded batch (the bench's own images). Both CPU legs of this
+    file call it, so they measure the same thing; the logits of the last step
+    come back under "logits"."""
     import torch
 
     from cutriton_b200 import workloads
@@ -609,14 +788,90 @@ def cpu_baseline(threads: int | None = None, batch: int = 8, steps: int = 2) -> 
     threads = threads or os.cpu_count() or 1
     torch.set_num_threads(threads)
     weights = workloads.resnet50_weights("baseline", seed=0)
-    x = workloads.resnet50_input(batch, seed=0)
-    torch_ref.resnet50_logits(x[:1], weights)  # warm-up
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        torch_ref.resnet50_logits(x, weights)
-    dt = time.perf_counter() - t0
-    return {"value": batch * steps / dt, "unit": "img/s", "cores": threads, "kind": "port",
-            "sample": f"PyTorch eager FP32 ResNet-50 on CPU, {steps} x batch {batch} (bounded sample of the bs256 step)"}
+    x = workloads.resnet50_input(batch, seed=0) if images is None else np.ascontiguousarray(images)
+    batch = x.shape[0]
+    torch_ref.resnet50_logits(x, weights)  # warm-up: one full step
+    times = []
+    t_end = time.perf_counter() + (seconds or 0.0)
+    while True:
+        t0 = time.perf_counter()
+        logits = torch_ref.resnet50_logits(x, weights)
+        times.append(time.perf_counter() - t0)
+        if steps is not None and len(times) >= steps:
+            break
+        if steps is None and len(times) >= 2 and time.perf_counter() >= t_end:
+            break
+    total = sum(times)
+    return {"value": batch * len(times) / total, "unit": "img/s", "cores": threads, "kind": "port",
+            "ms_per_step": total / len(times) * 1e3, "steps": len(times), "batch_per_step": batch,
+            "sample": f"PyTorch eager FP32 ResNet-50 on {threads} host threads, {len(times)} steps x {batch} images "
+                      f"(bounded sample of the bs{RN_BATCH_PER_GPU} step)", "logits": logits}
+
+
+def cpu_ffn(seconds: float = 3.0, threads: int | None = None, x: np.ndarray | None = None,
+            weights: dict | None = None) -> dict:
+    """The reference's PyTorch FFN (benchmarks/transformer_ffn_compare.py:52-60,
+    restated as the two-GEMM block of config 1) in FP16 on the host CPU,
+    full M=4096 per step; the output of the last step under "output"."""
+    import torch
+
+    from cutriton_b200 import workloads
+    from oracle import torch_ref
+
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    t, h, i = FFN["tokens"], FFN["hidden"], FFN["inner"]
+    w = weights if weights is not None else workloads.ffn_weights(h, i, seed=0)
+    x = x if x is not None else workloads.ffn_input(t, h, seed=0)
+    torch_ref.ffn_output(x, w, dtype=torch.float16)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while len(times) < 2 or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        out = torch_ref.ffn_output(x, w, dtype=torch.float16)
+        times.append(time.perf_counter() - t0)
+    med = float(np.median(times))
+    return {"value": t / med, "unit": "tokens/s", "cores": threads, "kind": "port", "dtype": "f16",
+            "sample": f"PyTorch eager FP16 FFN M={t} H={h} I={i} on {threads} host threads, median of {len(times)}",
+            "output": out}
+
+
+def cpu_baseline(rn: dict, ffn: dict | None, seconds: float = 10.0, timed: bool = True) -> dict:
+    """The CPU leg of the main line (rank 0). Times the reference's CPU path
+    for about `seconds` on the parity sample of this rank's own bs256 images
+    (and the FFN block on the bench's FFN input), and checks the GPU results
+    of the bench against those CPU results:
+
+    * ResNet-50 logits: max|d| <= 1e-3 * max|logit|, identical top-1;
+    * FFN output: max|d| <= 2e-2.
+
+    With `timed` False (N > 1) only the parity part runs and no baseline is
+    reported."""
+    picked = resnet_parity_sample(rn["logits"].shape[0])
+    cpu = cpu_resnet(None if timed else 1, len(picked), seconds=seconds if timed else None,
+                     images=rn["images"][picked])
+    ref = cpu.pop("logits").astype(np.float64)
+    got = rn["logits"][picked].astype(np.float64)
+    bound = 1e-3 * float(np.abs(ref).max())
+    err = float(np.abs(got - ref).max())
+    top1 = bool((got.argmax(axis=1) == ref.argmax(axis=1)).all())
+    parity = {"resnet50": {"images": picked.tolist(), "max_abs": err, "bound": bound, "top1_equal": top1,
+                           "pass": bool(err <= bound and top1 and np.isfinite(got).all()),
+                           "against": "PyTorch eager FP32 on the host (oracle/torch_ref.py)"}}
+    line = cpu if timed else {}
+    if ffn is not None:
+        fcpu = cpu_ffn(seconds=3.0 if timed else 0.0, x=ffn["input"], weights=ffn["weights"])
+        fref = fcpu.pop("output").astype(np.float64)
+        fgot = ffn["output"].astype(np.float64)
+        ferr = float(np.abs(fgot - fref).max())
+        parity["ffn"] = {"rows": int(fgot.shape[0]), "max_abs": ferr, "bound": 2e-2,
+                         "pass": bool(ferr <= 2e-2 and np.isfinite(fgot).all()),
+                         "against": "PyTorch eager FP16 on the host (oracle/torch_ref.py)"}
+        if timed:
+            line["ffn"] = fcpu
+    if timed:
+        line["host_cpu"] = host_cpu()
+    return {"baseline": line if timed else None, "parity": parity}
 
 
 def base_line(args, world) -> dict:
@@ -631,50 +886,45 @@ def base_line(args, world) -> dict:
     }
 
 
+def run_reference_arm(args) -> None:
+    """`--impl reference`: the reference's CPU comparison path (cpu_resnet) on
+    the host cores, rank 0 only; the other ranks of a torchrun launch exit
+    at once. Each step runs as many images of the bs256 step as keep the whole
+    run within about 150 s (all 256 when the host is fast enough)."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    probe = cpu_resnet(1, 8)
+    per_image_s = probe["ms_per_step"] / 1e3 / 8
+    budget_s = 150.0
+    batch = int(budget_s / max(1, args.steps) / per_image_s) // 8 * 8
+    batch = max(8, min(RN_BATCH_PER_GPU, batch))
+    cpu = cpu_resnet(args.steps, batch)
+    line = base_line(args, world)
+    line.update({"impl": "reference", "value": cpu["value"], "ms_per_step": cpu["ms_per_step"],
+                 "batch_per_step": batch, "gpus_used": 0,
+                 "compute": "host CPU on rank 0; the value does not depend on the number of GPUs launched",
+                 "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                 "host_cpu": host_cpu(),
+                 "e2e": {"value": cpu["value"], "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     args = parse_args()
     if args.profile_case:
         run_profile_case(args.profile_case)
         return
     if args.impl == "reference":
-        rank = int(os.environ.get("RANK", "0"))
-        world = int(os.environ.get("WORLD_SIZE", "1"))
-        if rank != 0:
-            return
-        line = base_line(args, world)
-        line["impl"] = "reference"
-        import torch
-
-        threads = os.cpu_count() or 1
-        torch.set_num_threads(threads)
-        from cutriton_b200 import workloads
-        from oracle import torch_ref
-
-        weights = workloads.resnet50_weights("baseline", seed=0)
-        batch = 8
-        x = workloads.resnet50_input(batch, seed=0)
-        for _ in range(max(1, min(args.warmup, 2))):
-            torch_ref.resnet50_logits(x[:2], weights)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            torch_ref.resnet50_logits(x, weights)
-        dt = time.perf_counter() - t0
-        value = batch * args.steps / dt
-        sample = f"PyTorch eager FP32 ResNet-50 on {threads} host threads, batch {batch} per step"
-        line.update({"value": value, "ms_per_step": dt / args.steps * 1e3,
-                     "config": {**line["config"], "batch_per_step": batch,
-                                "compute": "host CPU on rank 0 (no GPU used)"},
-                     "cpu_baseline": {"value": value, "unit": "img/s", "cores": threads, "kind": "port",
-                                      "sample": sample},
-                     "e2e": {"value": value, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
-        print(json.dumps(line), flush=True)
+        run_reference_arm(args)
         return
 
     world, rank, local = dist_setup(args)
     peaks, peak_kind = load_peaks()
     if args.config is not None:
         if args.config == 4:
-            line = run_config4(args, world, rank, local)
+            line = run_config4(args, world, rank, local, peaks, peak_kind)
         elif rank == 0:
             line = run_config2(args) if args.config == 2 else run_config3(args, peaks)
         else:
@@ -688,7 +938,8 @@ def main() -> None:
             dist.destroy_process_group()
         return
     rn = run_resnet(args, world, rank, local, peaks, peak_kind)
-    ffn = None if args.no_ffn else run_ffn(args, world, rank, local)
+    ffn = None if args.no_ffn else run_ffn(args, world, rank, local, peaks, peak_kind)
+    ffn4 = None if args.no_ffn else run_config4(args, world, rank, local, peaks, peak_kind)
     if rank == 0:
         line = base_line(args, world)
         line.update({"value": rn["value"], "ms_per_step": rn["ms_per_step"], "roofline": rn["roofline"],
@@ -697,9 +948,13 @@ def main() -> None:
         if "e2e" in rn:
             line["e2e"] = rn["e2e"]
         if ffn is not None:
-            line["ffn"] = ffn
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline()
+            line["ffn"] = {k: v for k, v in ffn.items() if k not in ("input", "output", "weights")}
+            line["ffn_config4"] = ffn4
+        if not args.no_cpu_baseline:
+            leg = cpu_baseline(rn, ffn, timed=(world == 1))
+            line["parity"] = leg["parity"]
+            if leg["baseline"] is not None:
+                line["cpu_baseline"] = leg["baseline"]
         line["peaks"] = peak_kind
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -108,6 +108,19 @@ extern "C" int ctb_gemm_f16_noalloc(const void* a, const void* b_t, void* c, int
   if (device < 0 || device >= kMaxDevices) {
     return Fail(error, error_len, CTB_NOALLOC_INVALID_ARGUMENT, "device ordinal out of range");
   }
+  if (stream != nullptr) {
+    // The scratch address, SM count and shared-memory opt-in below belong to
+    // the current device; a stream of another device would get the wrong ones.
+    int stream_device = -1;
+    status = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &stream_device);
+    if (status != cudaSuccess) return FailCuda(error, error_len, "cudaStreamGetDevice", status);
+    if (stream_device != device) {
+      char message[160];
+      std::snprintf(message, sizeof(message), "stream belongs to device %d but device %d is current",
+                    stream_device, device);
+      return Fail(error, error_len, CTB_NOALLOC_INVALID_ARGUMENT, message);
+    }
+  }
   DeviceSetup& setup = g_devices[device];
   {
     // Once per device, with that device current (it is: cudaGetDevice above).

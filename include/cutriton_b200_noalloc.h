@@ -12,7 +12,9 @@
  * a:   A, row-major [m, k] FP16, device pointer, 16-byte aligned
  * b_t: B transposed, row-major [n, k] FP16 (K-major), 16-byte aligned
  * c:   C, row-major [m, n] FP16, 16-byte aligned
- * k, n: multiples of 8. apply_gelu: 0 or 1. stream: a cudaStream_t (NULL = legacy).
+ * k, n: multiples of 8. apply_gelu: 0 or 1. stream: a cudaStream_t (NULL = legacy)
+ * of the current device; a stream of another device is rejected with
+ * CTB_NOALLOC_INVALID_ARGUMENT.
  * error/error_len: optional caller buffer for a message when the result is nonzero.
  *
  * Synchronous on `stream`; returns CTB_NOALLOC_OK (0) on success. The first

@@ -67,3 +67,25 @@ def test_reference_arm_under_torchrun_prints_one_line():
     line = json.loads(lines[0])
     assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["value"] > 0
     assert line["cpu_baseline"]["value"] == line["value"] and line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_cpu_leg_parity_check_passes_and_fails():
+    """The CPU leg's parity check of the bench's GPU logits, fed CPU logits
+    (pass) and the same logits with one entry pushed past the bound (fail)."""
+    import numpy as np
+
+    from cutriton_b200 import workloads
+    from oracle import torch_ref
+
+    batch = 16
+    images = workloads.resnet50_input(batch, seed=0)
+    picked = bench.resnet_parity_sample(batch)
+    assert picked.tolist() == list(range(16))
+    logits = np.zeros((batch, 1000), np.float32)
+    logits[picked] = torch_ref.resnet50_logits(images[picked], workloads.resnet50_weights("baseline", seed=0))
+    ok = bench.cpu_baseline({"images": images, "logits": logits}, None, timed=False)
+    assert ok["baseline"] is None and ok["parity"]["resnet50"]["pass"]
+    bad = logits.copy()
+    bad[3, 7] += 10 * ok["parity"]["resnet50"]["bound"] + 1.0
+    fail = bench.cpu_baseline({"images": images, "logits": bad}, None, timed=False)
+    assert not fail["parity"]["resnet50"]["pass"]

@@ -116,6 +116,30 @@ def test_max_pool_bitexact(cuda, shape):
         assert_bitexact(out["y"], expected, f"MaxPool {cand}")
 
 
+@pytest.mark.parametrize("shape", [(2, 8, 112, 112), (2, 5, 9, 13)])
+def test_max_pool_nan_bitexact(cuda, shape):
+    """NaN inputs: the reference's tl.maximum (resnet.py:178-180, default
+    propagate_nan=NONE, i.e. IEEE maxNum) returns the non-NaN operand, so a
+    NaN tap is skipped and a window of NaN taps only yields -inf (the
+    accumulator's start value). The oracle's `v > best` scan has the same
+    result; every candidate must match it bit for bit."""
+    x = randn(*shape)
+    x.flat[::5] = np.nan
+    x[0, 0, :3, :3] = np.nan   # output (0, 0, 0, 0): every in-range tap NaN
+    x[-1, -1, -3:, -3:] = np.nan
+    model = ct.Model()
+    model.add_input("x", list(shape))
+    model.add_node("pool", "MaxPool", ["x"], ["y"], kernel_shape=[3, 3], strides=[2, 2], pads=[1, 1, 1, 1],
+                   dilations=[1, 1])
+    model.add_output("y")
+    expected = oracle.max_pool(x)
+    assert expected[0, 0, 0, 0] == -np.inf and not np.isnan(expected).any()
+    engine = ct.build_engine(model)
+    for index, cand in enumerate(engine.ops()[0]["candidates"]):
+        out, _ = run_graph(model, {"x": x}, {"y": (expected.shape, np.float32)}, candidate=(0, index))
+        assert_bitexact(out["y"], expected, f"MaxPool NaN {cand}")
+
+
 @pytest.mark.parametrize("shape", [(4, 2048, 7, 7), (3, 17, 5, 3)])
 def test_global_average_pool(cuda, shape):
     x = randn(*shape)

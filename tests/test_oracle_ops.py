@@ -85,6 +85,30 @@ def test_max_pool_shapes_vs_torch(kernel, stride, pads, dilation):
     assert np.array_equal(ours, ref)  # a max is exact
 
 
+def test_max_pool_nan_is_maxnum():
+    """The reference reduces with tl.maximum(acc, tap) from acc = -inf
+    (resnet.py:171-181); its default NaN mode is IEEE maxNum, which returns
+    the non-NaN operand. np.fmax has the same rule, so a window reduction
+    with np.fmax from -inf is an independent statement of the reference."""
+    rng = np.random.default_rng(106)
+    x = rng.standard_normal((2, 3, 9, 10)).astype(np.float32)
+    x.flat[::4] = np.nan
+    x[0, 0, :2, :2] = np.nan  # the whole in-range window of output (0, 0, 0, 0)
+    ours = oracle.max_pool(x)
+    n, c, h, w = x.shape
+    oh, ow = (h - 1) // 2 + 1, (w - 1) // 2 + 1
+    expected = np.full((n, c, oh, ow), -np.inf, np.float32)
+    for i in range(oh):
+        for j in range(ow):
+            for a in range(3):
+                for b in range(3):
+                    ih, iw = 2 * i - 1 + a, 2 * j - 1 + b
+                    if 0 <= ih < h and 0 <= iw < w:
+                        expected[:, :, i, j] = np.fmax(expected[:, :, i, j], x[:, :, ih, iw])
+    assert np.array_equal(ours, expected)
+    assert ours[0, 0, 0, 0] == -np.inf
+
+
 def test_gemm_f32_vs_float64():
     rng = np.random.default_rng(105)
     a = rng.standard_normal((19, 67)).astype(np.float32)
