@@ -51,6 +51,8 @@ RUNTIME_SOURCES = [
     "compiler/compiler.cpp",
     "runtime/memory_planner.cpp",
     "runtime/profiler.cpp",
+    "runtime/device_session.cpp",
+    "runtime/tuner.cpp",
     "runtime/engine.cpp",
 ]
 

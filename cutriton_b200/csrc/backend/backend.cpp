@@ -65,115 +65,137 @@ Status TargetCapability(int device_id, int* capability) {
   return status;
 }
 
-Status CheckTensor(const Graph& graph, const std::string& name, const Device& device) {
+// Why the value `name` cannot take part in a cuda_sm100 launch, or "".
+std::string TensorProblem(const Graph& graph, const std::string& name, const Device& device) {
   const ValueDesc* value = graph.FindValue(name);
-  if (value == nullptr) return Status::NotFound("tensor description is missing: " + name);
-  CUTRITON_RETURN_IF_ERROR(value->tensor.Validate());
-  if (value->tensor.dtype != DataType::kFloat32 && value->tensor.dtype != DataType::kFloat16) {
-    return Status::Unsupported("only float32/float16 tensors are supported: " + name);
+  if (value == nullptr) return "'" + name + "' has no description";
+  const Status valid = value->tensor.Validate();
+  if (!valid.ok()) return "'" + name + "': " + valid.message();
+  const DataType dtype = value->tensor.dtype;
+  if (dtype != DataType::kFloat32 && dtype != DataType::kFloat16) {
+    return "'" + name + "' is " + DataTypeName(dtype) + " (kernels take float32 / float16)";
   }
   if (value->tensor.device_type != device.type || value->tensor.device_id != device.id) {
-    return Status::Unsupported("tensor is assigned to another device: " + name);
+    return "'" + name + "' is placed on another device";
   }
-  return Status::OK();
+  return "";
 }
 
 bool ConstraintHolds(const KernelConstraint& c, const Node& node, const ValueLookup& lookup) {
+  const auto pick = [&](bool output) -> const ValueDesc* {
+    const auto& names = output ? node.outputs() : node.inputs();
+    if (c.tensor_index < 0 || static_cast<std::size_t>(c.tensor_index) >= names.size()) return nullptr;
+    return lookup(names[static_cast<std::size_t>(c.tensor_index)]);
+  };
   switch (c.kind) {
     case KernelConstraintKind::kInputCountEquals:
-      return node.inputs().size() == static_cast<std::size_t>(c.expected);
+      return static_cast<int64_t>(node.inputs().size()) == c.expected;
     case KernelConstraintKind::kAttributeInt64Equals:
       return GetIntAttribute(node, c.attribute_name, c.default_value) == c.expected;
     case KernelConstraintKind::kAttributeListEquals:
       return GetIntListAttribute(node, c.attribute_name, c.default_list) == c.expected_list;
     case KernelConstraintKind::kInputIsConstant: {
-      if (c.tensor_index < 0 || static_cast<std::size_t>(c.tensor_index) >= node.inputs().size()) return false;
-      const ValueDesc* v = lookup(node.inputs()[static_cast<std::size_t>(c.tensor_index)]);
+      const ValueDesc* v = pick(false);
       return v != nullptr && v->is_constant;
     }
-    case KernelConstraintKind::kTensorRankEquals:
+    case KernelConstraintKind::kTensorRankEquals: {
+      const ValueDesc* v = pick(c.tensor_is_output);
+      return v != nullptr && static_cast<int64_t>(v->tensor.shape.size()) == c.expected;
+    }
     case KernelConstraintKind::kDimMultipleOf:
     case KernelConstraintKind::kDimLessEqual: {
-      const auto& names = c.tensor_is_output ? node.outputs() : node.inputs();
-      if (c.tensor_index < 0 || static_cast<std::size_t>(c.tensor_index) >= names.size()) return false;
-      const ValueDesc* v = lookup(names[static_cast<std::size_t>(c.tensor_index)]);
-      if (v == nullptr) return false;
-      const auto& shape = v->tensor.shape;
-      if (c.kind == KernelConstraintKind::kTensorRankEquals) {
-        return shape.size() == static_cast<std::size_t>(c.expected);
-      }
-      if (c.axis < 0 || static_cast<std::size_t>(c.axis) >= shape.size()) return false;
-      const int64_t dim = shape[static_cast<std::size_t>(c.axis)];
-      return c.kind == KernelConstraintKind::kDimMultipleOf ? dim % c.expected == 0
-                                                           : dim <= c.expected;
+      const ValueDesc* v = pick(c.tensor_is_output);
+      if (v == nullptr || c.axis < 0 || static_cast<std::size_t>(c.axis) >= v->tensor.shape.size()) return false;
+      const int64_t dim = v->tensor.shape[static_cast<std::size_t>(c.axis)];
+      return c.kind == KernelConstraintKind::kDimMultipleOf ? dim % c.expected == 0 : dim <= c.expected;
     }
   }
   return false;
 }
 
-bool ArtifactMatches(const KernelArtifact& artifact, const Node& node, const ValueLookup& lookup,
-                     int capability) {
-  if (capability < artifact.min_compute_capability) return false;
-  const std::string& reference_name = node.outputs().empty() ? node.inputs().front() : node.outputs().front();
-  const ValueDesc* reference = lookup(reference_name);
-  if (reference == nullptr || artifact.dtype != DataTypeName(reference->tensor.dtype)) return false;
-  auto layout_ok = [&](const std::string& name) {
+// Why pack variant `artifact` cannot run `node` on a device of compute
+// capability `capability`, or "" when it can. Checked in order: SM, the
+// element type of the node's first output (first input for output-less
+// nodes), the layout of the first input and of every output, prepacked
+// arguments binding constants, then every constraint of the entry.
+std::string VariantProblem(const KernelArtifact& artifact, const Node& node, const ValueLookup& lookup,
+                           int capability) {
+  if (capability < artifact.min_compute_capability) {
+    return "needs sm_" + std::to_string(artifact.min_compute_capability);
+  }
+  const std::string& typed = node.outputs().empty() ? node.inputs().front() : node.outputs().front();
+  const ValueDesc* typed_value = lookup(typed);
+  if (typed_value == nullptr) return "'" + typed + "' has no description";
+  if (artifact.dtype != DataTypeName(typed_value->tensor.dtype)) return "is a " + artifact.dtype + " kernel";
+  std::vector<std::string> laid_out(node.outputs().begin(), node.outputs().end());
+  if (!node.inputs().empty()) laid_out.push_back(node.inputs().front());
+  for (const std::string& name : laid_out) {
     const ValueDesc* v = lookup(name);
-    return v != nullptr && (artifact.layout.empty() || v->tensor.layout == artifact.layout);
-  };
-  if (!node.inputs().empty() && !layout_ok(node.inputs().front())) return false;
-  for (const auto& output : node.outputs()) {
-    if (!layout_ok(output)) return false;
+    if (v == nullptr) return "'" + name + "' has no description";
+    if (!artifact.layout.empty() && v->tensor.layout != artifact.layout) {
+      return "wants layout " + artifact.layout + " for '" + name + "'";
+    }
   }
-  // A prepacked argument can only bind a constant input.
-  for (const auto& arg : artifact.arguments) {
-    if (arg.source.prepack.empty()) continue;
-    if (arg.source.index < 0 || static_cast<std::size_t>(arg.source.index) >= node.inputs().size()) return false;
-    const ValueDesc* v = lookup(node.inputs()[static_cast<std::size_t>(arg.source.index)]);
-    if (v == nullptr || !v->is_constant) return false;
+  for (const auto& argument : artifact.arguments) {
+    if (argument.source.prepack.empty()) continue;
+    const int slot = argument.source.index;
+    const ValueDesc* v =
+        slot >= 0 && static_cast<std::size_t>(slot) < node.inputs().size() ? lookup(node.inputs()[slot]) : nullptr;
+    if (v == nullptr || !v->is_constant) return "prepacks argument '" + argument.name + "', which is not a constant";
   }
-  return std::all_of(artifact.constraints.begin(), artifact.constraints.end(),
-                     [&](const KernelConstraint& c) { return ConstraintHolds(c, node, lookup); });
+  for (std::size_t i = 0; i < artifact.constraints.size(); ++i) {
+    if (!ConstraintHolds(artifact.constraints[i], node, lookup)) return "constraint " + std::to_string(i) + " fails";
+  }
+  return "";
 }
 
+bool ArtifactMatches(const KernelArtifact& artifact, const Node& node, const ValueLookup& lookup, int capability) {
+  return VariantProblem(artifact, node, lookup, capability).empty();
+}
+
+// Node-level admission for cuda_sm100: a CUDA device, a schema whose arity
+// the node meets, float tensors on the plan's device, and either a pack
+// variant that can run it or (fused ops) a registered decomposition.
+// `capability` receives the target's compute capability.
 Status CheckCudaNode(const Node& node, const Graph& graph, const BackendOptions& options,
                      const ArtifactRepository& repository, int* capability) {
-  if (options.device.type != DeviceType::kCUDA) {
-    return Status::Unsupported("cuda_sm100 requires a CUDA device");
-  }
+  const std::string who = "cuda_sm100, node '" + node.name() + "' (" + node.op_type() + "): ";
+  if (options.device.type != DeviceType::kCUDA) return Status::Unsupported(who + "the plan is not on a CUDA device");
   CUTRITON_RETURN_IF_ERROR(RegisterBuiltinOpSchemas());
   const auto schema = OpSchemaRegistry::Global().Find(node.op_type());
-  if (schema == nullptr) return Status::Unsupported("no op schema is registered for " + node.op_type());
-  if (node.inputs().size() < schema->min_inputs || node.inputs().size() > schema->max_inputs ||
-      node.outputs().size() != schema->outputs) {
-    return Status::Unsupported(node.op_type() + " has an invalid input/output count");
+  if (schema == nullptr) return Status::Unsupported(who + "unknown op type");
+  const std::size_t ins = node.inputs().size();
+  if (ins < schema->min_inputs || ins > schema->max_inputs || node.outputs().size() != schema->outputs) {
+    return Status::Unsupported(who + "wrong number of inputs or outputs");
   }
-  for (const auto& name : node.inputs()) CUTRITON_RETURN_IF_ERROR(CheckTensor(graph, name, options.device));
-  for (const auto& name : node.outputs()) CUTRITON_RETURN_IF_ERROR(CheckTensor(graph, name, options.device));
+  for (const auto* names : {&node.inputs(), &node.outputs()}) {
+    for (const std::string& name : *names) {
+      const std::string problem = TensorProblem(graph, name, options.device);
+      if (!problem.empty()) return Status::Unsupported(who + problem);
+    }
+  }
   if (node.op_type() == "Flatten") {
-    const auto& outs = graph.outputs();
-    if (std::find(outs.begin(), outs.end(), node.outputs().front()) != outs.end()) {
-      return Status::Unsupported("a Flatten graph output would need an explicit copy kernel");
+    const auto& outputs = graph.outputs();
+    if (std::find(outputs.begin(), outputs.end(), node.outputs().front()) != outputs.end()) {
+      return Status::Unsupported(who + "a Flatten that is a graph output would need a copy kernel");
     }
     return Status::OK();
   }
-  const auto* artifacts = repository.Find(node.op_type());
-  if (artifacts == nullptr || artifacts->empty()) {
-    // A fused op without its own kernel may still lower through its
-    // decomposition; Lower decides.
-    if (FusionRegistry::Global().Find(node.op_type()).empty()) {
-      return Status::Unsupported("no Kernel Pack entry for " + node.op_type());
-    }
+  const bool decomposable = !FusionRegistry::Global().Find(node.op_type()).empty();
+  const auto* variants = repository.Find(node.op_type());
+  if ((variants == nullptr || variants->empty()) && !decomposable) {
+    return Status::Unsupported(who + "the kernel pack has no entry for this op");
   }
   CUTRITON_RETURN_IF_ERROR(TargetCapability(options.device.id, capability));
-  if (artifacts == nullptr) return Status::OK();
+  if (variants == nullptr || decomposable) return Status::OK();
   const ValueLookup lookup = [&](const std::string& n) { return graph.FindValue(n); };
-  for (const auto& artifact : *artifacts) {
-    if (ArtifactMatches(artifact, node, lookup, *capability)) return Status::OK();
+  std::string reasons;
+  for (const KernelArtifact& variant : *variants) {
+    const std::string problem = VariantProblem(variant, node, lookup, *capability);
+    if (problem.empty()) return Status::OK();
+    reasons += (reasons.empty() ? "" : "; ") + variant.identity() + " " + problem;
   }
-  if (!FusionRegistry::Global().Find(node.op_type()).empty()) return Status::OK();
-  return Status::Unsupported("no Kernel Pack variant of " + node.op_type() +
-                             " matches dtype/layout/SM/constraints");
+  return Status::Unsupported(who + "no pack variant fits: " + reasons);
 }
 
 // Kernel for one step of an unfused decomposition: the default variant if its

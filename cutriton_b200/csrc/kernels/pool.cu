@@ -7,8 +7,16 @@
 // 3x3/2 windows of neighbouring threads overlap, so input rows are served
 // from L1 and HBM traffic stays near input + output bytes.
 //
-// GlobalAveragePool (resnet.py:185-198): one warp per (n, c) plane, lanes
-// stride the plane, warp-shuffle sum, then divide by H*W.
+// GlobalAveragePool (resnet.py:185-198): the reference sums each plane
+// serially, then divides by H*W. Two kernels:
+//   * ctb_global_average_pool_f32_staged (planes of at most 81 elements, the
+//     7x7 ResNet case): a block copies 128 consecutive planes — one
+//     contiguous run of NCHW memory — into shared memory with 16-byte
+//     cp.async copies (every thread keeps several in flight), then each
+//     thread sums one plane in the reference's order, so results are
+//     bit-identical to a serial FP32 loop;
+//   * ctb_global_average_pool_f32 (any plane size): one warp per plane,
+//     lanes stride the plane, warp-shuffle sum, then the division.
 
 #include <math_constants.h>
 
@@ -102,5 +110,49 @@ ctb_max_pool_3x3s2_f32(const float* __restrict__ x, float* __restrict__ out, int
     float* dst = out + row * out_w + 2 * lane;
     dst[0] = o0;
     dst[1] = o1;
+  }
+}
+
+// Planes per block and the largest plane the staged kernel takes.
+constexpr int kGapPlanes = 128;
+constexpr int kGapMaxSpatial = 81;
+
+extern "C" __global__ void __launch_bounds__(kGapPlanes)
+ctb_global_average_pool_f32_staged(const float* __restrict__ x, float* __restrict__ out, int n, int c, int h, int w,
+                                   CTB_RESERVED_PARAMS) {
+  CTB_UNUSED_RESERVED();
+  CTB_GRID_DEPENDENCY_SYNC();
+  __shared__ __align__(16) float stage[kGapPlanes * kGapMaxSpatial];
+  const int spatial = h * w;
+  const long long planes = static_cast<long long>(n) * c;
+  const long long first = static_cast<long long>(blockIdx.x) * kGapPlanes;
+  const int count = static_cast<int>(min(static_cast<long long>(kGapPlanes), planes - first));
+  const float* src = x + first * spatial;
+  const int elems = count * spatial;
+  // 16-byte copies when the run starts on a 16-byte boundary (always for
+  // an aligned tensor: first * spatial is a multiple of 128); the ragged
+  // end, or a misaligned tensor, goes 4 bytes at a time.
+  const bool vector_ok = (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+  const int vec = vector_ok ? elems / 4 : 0;
+  for (int i = threadIdx.x; i < vec; i += kGapPlanes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
+                     __cvta_generic_to_shared(stage + 4 * i))),
+                 "l"(src + 4 * i)
+                 : "memory");
+  }
+  for (int i = 4 * vec + threadIdx.x; i < elems; i += kGapPlanes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(
+                     __cvta_generic_to_shared(stage + i))),
+                 "l"(src + i)
+                 : "memory");
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  if (threadIdx.x < count) {
+    // Row stride `spatial` (odd for 7x7): consecutive threads hit distinct banks.
+    const float* plane = stage + threadIdx.x * spatial;
+    float sum = 0.0f;
+    for (int i = 0; i < spatial; ++i) sum += plane[i];
+    out[first + threadIdx.x] = sum / static_cast<float>(spatial);
   }
 }

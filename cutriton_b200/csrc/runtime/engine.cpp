@@ -1,376 +1,125 @@
-// Engine / ExecutionContext: binding, shape profiles, workspace views,
-// candidate tuning with an on-disk cache, CUDA Graph capture with an LRU of
-// instantiated graphs, per-op event profiling and the device error block.
+// Engine and ExecutionContext.
 //
-// Semantics follow the reference runtime (src/runtime/engine.cpp): binding
-// validation 86-111/426-472, profiles 486-571, PrepareTensors 593-668,
-// PrepareKernels 670-723, PrepareTuning 725-891 (FNV-1a tuning key 215-295,
-// atomic JSON cache 297-335), RunAsync 925-1079 and Synchronize 1081-1119.
-// Added here: constant prepacking at upload, and the error block — a small
-// pinned, device-mapped host buffer bound to each kernel's first
-// runtime_reserved parameter; kernels with bounded spin-waits record an
-// expired wait there instead of hanging, and Synchronize reports it.
+// Engine holds the compiled plan and, in EngineState, what every context of
+// it shares: device copies of the constants (plus their prepacked forms,
+// derived once at upload) and the CUDA module cache. Both are created on
+// first use, once.
+//
+// An ExecutionContext keeps all of its mutable state in one Session. Staleness
+// is tracked with epochs instead of a flag per stage: changing the shape
+// profile or an input shape bumps the layout epoch, binding a graph-boundary
+// tensor bumps the binding epoch, pinning a candidate bumps the choice epoch.
+// Each stage remembers the epochs it was built at and rebuilds when they
+// moved:
+//
+//   tensor table   layout, binding   constants + workspace views + bindings
+//   selection      layout, choice    default / pinned / tuned candidate per op
+//   kernels        layout, choice    OpKernels of the selected candidates
+//
+// RunAsync on a CUDA plan enqueues the kernels directly, or — with CUDA
+// Graphs on — replays the graph captured for the current launch fingerprint
+// (profile, workspace, bound addresses and shapes, selected candidates) from
+// an LRU GraphCache. Kernels get the DeviceSession's error word as their
+// runtime scratch; Synchronize reports an expired bounded wait from it.
 
 #include "cutriton/runtime/engine.h"
 
 #include <algorithm>
-#include <cmath>
-#include <cstdint>
-#include <cstring>
-#include <filesystem>
-#include <fstream>
-#include <iomanip>
-#include <limits>
 #include <mutex>
 #include <optional>
-#include <sstream>
-#include <type_traits>
 #include <variant>
 
 #include "../backend/prepack.h"
 #include "../cuda_driver.h"
 #include "cutriton/core/buffer.h"
 #include "cutriton/ir/pass.h"
+#include "device_session.h"
+#include "tuner.h"
 
 namespace cutriton {
-namespace {
 
-bool Contains(const std::vector<std::string>& list, const std::string& name) {
-  return std::find(list.begin(), list.end(), name) != list.end();
-}
-
-// IEEE binary16 -> binary32 (exact).
-float HalfToFloat(std::uint16_t h) {
-  const std::uint32_t sign = std::uint32_t(h & 0x8000u) << 16;
-  const std::uint32_t exp = (h >> 10) & 0x1Fu;
-  std::uint32_t man = h & 0x3FFu;
-  std::uint32_t bits;
-  if (exp == 0x1Fu) {
-    bits = sign | 0x7F800000u | (man << 13);
-  } else if (exp != 0) {
-    bits = sign | ((exp + 112u) << 23) | (man << 13);
-  } else if (man == 0) {
-    bits = sign;
-  } else {
-    int e = -1;
-    do { man <<= 1; ++e; } while ((man & 0x400u) == 0);
-    bits = sign | (std::uint32_t(112 - e) << 23) | ((man & 0x3FFu) << 13);
-  }
-  float f;
-  std::memcpy(&f, &bits, sizeof f);
-  return f;
-}
-
-Status ValidateBoundTensor(const std::string& name, const TensorDesc& expected, const Tensor& tensor) {
-  CUTRITON_RETURN_IF_ERROR(tensor.desc().Validate());
-  if (!tensor.defined() || tensor.buffer()->empty()) {
-    return Status::InvalidArgument("tensor buffer is not defined: " + name);
-  }
-  const TensorDesc& actual = tensor.desc();
-  if (actual.shape != expected.shape || actual.dtype != expected.dtype ||
-      actual.layout != expected.layout || actual.device_type != expected.device_type ||
-      actual.device_id != expected.device_id) {
-    return Status::InvalidArgument("tensor description does not match the plan: " + name);
-  }
-  if (tensor.buffer()->device_type() != expected.device_type ||
-      tensor.buffer()->device_id() != expected.device_id) {
-    return Status::InvalidArgument("tensor buffer is on the wrong device: " + name);
-  }
-  if (tensor.byte_offset() > tensor.buffer()->size_bytes() ||
-      expected.ByteSize() > tensor.buffer()->size_bytes() - tensor.byte_offset()) {
-    return Status::InvalidArgument("tensor buffer is too small: " + name);
-  }
-  return Status::OK();
-}
-
-Status CopyAsFloat(const Tensor& tensor, std::vector<float>* out) {
-  const auto count = static_cast<std::size_t>(tensor.desc().NumElements());
-  out->assign(count, 0.0f);
-  if (tensor.desc().dtype == DataType::kFloat32) {
-    return tensor.buffer()->CopyToHost(out->data(), tensor.desc().ByteSize(), tensor.byte_offset());
-  }
-  if (tensor.desc().dtype == DataType::kFloat16) {
-    std::vector<std::uint16_t> half(count);
-    CUTRITON_RETURN_IF_ERROR(tensor.buffer()->CopyToHost(half.data(), tensor.desc().ByteSize(), tensor.byte_offset()));
-    for (std::size_t i = 0; i < count; ++i) (*out)[i] = HalfToFloat(half[i]);
-    return Status::OK();
-  }
-  return Status::Unsupported("tuning comparison supports float32/float16 only");
-}
-
-struct EventPair {
-  CUevent start{nullptr};
-  CUevent end{nullptr};
-  bool timed{false};
-};
-
-struct GraphEntry {
-  std::string key;
-  CUgraph graph{nullptr};
-  CUgraphExec exec{nullptr};
-  std::uint64_t last_used{0};
-};
-
-// Layout of the error block shared with kernels (see kernels/common.cuh).
-struct ErrorBlock {
-  std::uint32_t code;     // 0 = no error
-  std::uint32_t site;     // kernel-defined location of the expired wait
-  std::uint32_t block;    // linear CTA index that gave up
-  std::uint32_t reserved[13];
-};
-
-struct CudaState {
-  CUdevice device{};
-  CUcontext context{nullptr};
-  CUstream owned_stream{nullptr};
-  CUstream active_stream{nullptr};
-  std::vector<GraphEntry> graphs;
-  std::uint64_t clock{0};
-  std::vector<EventPair> events;
-  ErrorBlock* error_host{nullptr};
-  CUdeviceptr error_device{0};
-};
-
-void DestroyGraphs(CudaState* s) {
-  const auto& api = drv::Get();
-  for (auto& g : s->graphs) {
-    if (g.exec != nullptr) api.cuGraphExecDestroy(g.exec);
-    if (g.graph != nullptr) api.cuGraphDestroy(g.graph);
-  }
-  s->graphs.clear();
-}
-
-void DestroyCudaState(CudaState* s) {
-  if (s == nullptr) return;
-  const auto& api = drv::Get();
-  if (s->context != nullptr) api.cuCtxSetCurrent(s->context);
-  DestroyGraphs(s);
-  for (auto& e : s->events) {
-    if (e.start != nullptr) api.cuEventDestroy(e.start);
-    if (e.end != nullptr) api.cuEventDestroy(e.end);
-  }
-  if (s->owned_stream != nullptr) api.cuStreamDestroy(s->owned_stream);
-  if (s->error_host != nullptr) api.cuMemFreeHost(s->error_host);
-  if (s->context != nullptr) api.cuDevicePrimaryCtxRelease(s->device);
-  delete s;
-}
-
-Status InitializeCudaState(CudaState* s, int device_id, std::size_t ops, bool profiling) {
-  CUTRITON_RETURN_IF_ERROR(drv::RetainPrimaryContext(device_id, &s->device, &s->context));
-  const auto& api = drv::Get();
-  CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuStreamCreate(&s->owned_stream, CU_STREAM_NON_BLOCKING), "cuStreamCreate"));
-  void* host = nullptr;
-  CUTRITON_RETURN_IF_ERROR(drv::Check(
-      api.cuMemHostAlloc(&host, sizeof(ErrorBlock), CU_MEMHOSTALLOC_DEVICEMAP | CU_MEMHOSTALLOC_PORTABLE),
-      "cuMemHostAlloc"));
-  s->error_host = static_cast<ErrorBlock*>(host);
-  std::memset(s->error_host, 0, sizeof(ErrorBlock));
-  CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuMemHostGetDevicePointer(&s->error_device, host, 0),
-                                      "cuMemHostGetDevicePointer"));
-  s->events.resize(ops);
-  if (profiling) {
-    for (auto& e : s->events) {
-      CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuEventCreate(&e.start, CU_EVENT_DEFAULT), "cuEventCreate"));
-      CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuEventCreate(&e.end, CU_EVENT_DEFAULT), "cuEventCreate"));
-    }
-  }
-  return Status::OK();
-}
-
-std::string Hex64(std::uint64_t v) {
-  std::ostringstream out;
-  out << std::hex << std::setw(16) << std::setfill('0') << v;
-  return out.str();
-}
-
-// Tuning cache key: FNV-1a 64 over the op, its tensors (dtype, layout,
-// shape), its attributes, every candidate's kernel identity and binary hash,
-// and the device (SM, UUID) and driver version.
-std::string TuningKey(const PlanOp& op, const Node& node, const Graph& graph, int device_id) {
-  std::ostringstream m;
-  m << op.op_type << '|' << device_id;
-  auto tensors = [&](const char* role, const std::vector<std::string>& names) {
-    for (const auto& name : names) {
-      m << '|' << role << ':' << name;
-      if (const ValueDesc* v = graph.FindValue(name)) {
-        m << ':' << static_cast<int>(v->tensor.dtype) << ':' << v->tensor.layout;
-        for (int64_t d : v->tensor.shape) m << ':' << d;
-      }
-    }
-  };
-  tensors("input", op.inputs);
-  tensors("output", op.outputs);
-  std::vector<std::string> keys;
-  for (const auto& a : node.attributes()) keys.push_back(a.first);
-  std::sort(keys.begin(), keys.end());
-  for (const auto& k : keys) {
-    const Attribute& attr = node.attributes().at(k);
-    m << "|attribute:" << k << ':' << attr.index();
-    std::visit([&](const auto& v) {
-      using T = std::decay_t<decltype(v)>;
-      if constexpr (std::is_same_v<T, std::vector<int64_t>> || std::is_same_v<T, std::vector<double>>) {
-        for (const auto& x : v) m << ':' << x;
-      } else {
-        m << ':' << v;
-      }
-    }, attr);
-  }
-  for (const auto& c : op.candidates) {
-    m << '|' << c.candidate_id;
-    for (const auto& step : c.steps) {
-      if (const auto* inv = std::get_if<KernelInvocation>(&step)) {
-        const KernelArtifact& a = inv->artifact;
-        m << "|pack:" << a.pack_name << ':' << a.pack_version << "|kernel:" << a.kernel_id << ':'
-          << a.kernel_version << ':' << a.variant_id << "|abi:" << a.abi_schema_version
-          << "|generator:" << a.generator_version << "|binary:" << a.sha256;
-      } else {
-        m << "|view";
-      }
-    }
-  }
-  const auto& api = drv::Get();
-  CUdevice device{};
-  if (api.available && api.cuDeviceGet(&device, device_id) == CUDA_SUCCESS) {
-    int major = 0, minor = 0;
-    CUuuid uuid{};
-    api.cuDeviceGetUuid(&uuid, device);
-    api.cuDeviceGetAttribute(&major, CU_DEVICE_ATTRIBUTE_COMPUTE_CAPABILITY_MAJOR, device);
-    api.cuDeviceGetAttribute(&minor, CU_DEVICE_ATTRIBUTE_COMPUTE_CAPABILITY_MINOR, device);
-    m << "|sm:" << major << minor << "|uuid:" << std::hex;
-    for (char b : uuid.bytes) m << static_cast<int>(static_cast<unsigned char>(b));
-    m << std::dec;
-  }
-  int driver = 0;
-  if (api.available) api.cuDriverGetVersion(&driver);
-  m << "|driver:" << driver;
-  std::uint64_t h = 14695981039346656037ull;
-  for (unsigned char c : m.str()) {
-    h ^= c;
-    h *= 1099511628211ull;
-  }
-  return Hex64(h);
-}
-
-std::optional<std::string> ReadTuningChoice(const std::filesystem::path& path) {
-  std::ifstream in(path);
-  if (!in) return std::nullopt;
-  std::ostringstream text;
-  text << in.rdbuf();
-  const std::string s = text.str();
-  const std::string marker = "\"candidate_id\": \"";
-  const auto begin = s.find(marker);
-  if (begin == std::string::npos) return std::nullopt;
-  const auto start = begin + marker.size();
-  const auto end = s.find('"', start);
-  if (end == std::string::npos) return std::nullopt;
-  return s.substr(start, end - start);
-}
-
-// Writes to a temporary file and renames it over the target (atomic publish).
-Status WriteTuningChoice(const std::filesystem::path& path, const std::string& key,
-                         const std::string& candidate_id, double median_ms) {
-  std::error_code error;
-  std::filesystem::create_directories(path.parent_path(), error);
-  if (error) return Status::RuntimeError("cannot create the tuning cache directory: " + error.message());
-  const std::string temporary = path.string() + ".tmp";
-  {
-    std::ofstream out(temporary, std::ios::trunc);
-    out << "{\n  \"schema_version\": 1,\n  \"tuning_key\": \"" << key << "\",\n  \"candidate_id\": \""
-        << candidate_id << "\",\n  \"median_ms\": " << median_ms << "\n}\n";
-    if (!out) return Status::RuntimeError("cannot write the tuning cache");
-  }
-  std::filesystem::rename(temporary, path, error);
-  if (error) {
-    std::filesystem::remove(path, error);
-    error.clear();
-    std::filesystem::rename(temporary, path, error);
-  }
-  return error ? Status::RuntimeError("cannot publish the tuning cache: " + error.message()) : Status::OK();
-}
-
-std::optional<std::size_t> CandidateIndex(const PlanOp& op, const std::string& id) {
-  for (std::size_t i = 0; i < op.candidates.size(); ++i) {
-    if (op.candidates[i].candidate_id == id) return i;
-  }
-  return std::nullopt;
-}
-
-}  // namespace
+// ---- shared engine state ---------------------------------------------------------
 
 class EngineState {
  public:
-  explicit EngineState(ExecutablePlan p) : plan(std::move(p)) {}
+  explicit EngineState(ExecutablePlan compiled) : plan(std::move(compiled)) {}
 
-  Status InitializeConstants() {
-    std::call_once(constants_once_, [&]() { constants_status_ = UploadConstants(); });
+  bool on_cuda() const { return plan.backend_options().device.type == DeviceType::kCUDA; }
+  int device_id() const { return plan.backend_options().device.id; }
+
+  // Device constants (host tensors as they are for CPU plans).
+  Status Constants(const std::unordered_map<std::string, Tensor>** out) {
+    std::call_once(constants_once_, [this]() { constants_status_ = BuildConstants(); });
+    *out = &constants_;
     return constants_status_;
   }
 
-  Status InitializeModuleCache() {
-    if (plan.backend_options().device.type != DeviceType::kCUDA) return Status::OK();
-    std::call_once(cache_once_, [&]() {
-      cache_status_ = CreateCudaModuleCache(plan.backend_options().device.id, &module_cache);
-    });
-    return cache_status_;
+  Status Modules(std::shared_ptr<CudaModuleCache>* out) {
+    if (on_cuda()) {
+      std::call_once(modules_once_, [this]() { modules_status_ = CreateCudaModuleCache(device_id(), &modules_); });
+    }
+    *out = modules_;
+    return modules_status_;
   }
 
-  ExecutablePlan plan;
-  std::unordered_map<std::string, Tensor> device_constants;
-  std::shared_ptr<CudaModuleCache> module_cache;
+  std::size_t module_count() const { return LoadedModuleCount(modules_); }
+
+  const ExecutablePlan plan;
 
  private:
-  Status Upload(const std::string& name, const TensorDesc& desc, const void* bytes) {
+  Status Place(const std::string& name, TensorDesc desc, const void* host_bytes) {
+    desc.device_type = DeviceType::kCUDA;
+    desc.device_id = device_id();
     std::shared_ptr<Buffer> buffer;
-    CUTRITON_RETURN_IF_ERROR(Buffer::AllocateCuda(desc.ByteSize(), plan.backend_options().device.id, &buffer));
-    CUTRITON_RETURN_IF_ERROR(buffer->CopyFromHost(bytes, desc.ByteSize()));
-    device_constants[name] = Tensor(desc, std::move(buffer));
+    CUTRITON_RETURN_IF_ERROR(Buffer::AllocateCuda(desc.ByteSize(), device_id(), &buffer));
+    CUTRITON_RETURN_IF_ERROR(buffer->CopyFromHost(host_bytes, desc.ByteSize()));
+    constants_[name] = Tensor(std::move(desc), std::move(buffer));
     return Status::OK();
   }
 
-  Status UploadConstants() {
-    const bool cpu = plan.backend_options().device.type == DeviceType::kCPU;
-    for (const auto& entry : plan.constants()) {
-      const ValueDesc* value = plan.graph().FindValue(entry.first);
+  static const std::uint8_t* HostBytes(const Tensor& t) {
+    return static_cast<const std::uint8_t*>(t.buffer()->data()) + t.byte_offset();
+  }
+
+  Status BuildConstants() {
+    for (const auto& [name, host] : plan.constants()) {
+      const ValueDesc* value = plan.graph().FindValue(name);
       if (value == nullptr || !value->is_constant) {
-        return Status::Internal("plan constant is missing from the graph: " + entry.first);
+        return Status::Internal("plan constant '" + name + "' is not a constant of the graph");
       }
-      if (cpu) {
-        device_constants.emplace(entry.first, entry.second);
+      if (!on_cuda()) {
+        constants_.emplace(name, host);
         continue;
       }
-      const Tensor& source = entry.second;
-      const auto* bytes = static_cast<const std::uint8_t*>(source.buffer()->data()) + source.byte_offset();
-      CUTRITON_RETURN_IF_ERROR(Upload(entry.first, value->tensor, bytes));
+      CUTRITON_RETURN_IF_ERROR(Place(name, value->tensor, HostBytes(host)));
     }
-    if (cpu) return Status::OK();
-    // Derived constants for every prepacked argument of every candidate.
-    for (const auto& op : plan.ops()) {
-      for (const auto& candidate : op.candidates) {
-        for (const auto& step : candidate.steps) {
-          const auto* inv = std::get_if<KernelInvocation>(&step);
-          if (inv == nullptr) continue;
-          for (const auto& arg : inv->artifact.arguments) {
-            if (arg.source.prepack.empty()) continue;
-            const auto index = static_cast<std::size_t>(arg.source.index);
-            if (index >= inv->inputs.size()) return Status::Internal("prepack argument index is invalid");
-            const std::string& base = inv->inputs[index];
-            const std::string derived = PrepackedName(base, arg.source.prepack);
-            if (device_constants.count(derived) != 0) continue;
-            const auto found = plan.constants().find(base);
-            if (found == plan.constants().end()) {
-              return Status::InvalidArgument("prepacked argument does not bind a constant: " + base);
+    if (!on_cuda()) return Status::OK();
+    // Prepacked forms named by kernel arguments of any candidate.
+    for (const PlanOp& op : plan.ops()) {
+      for (const ExecutionCandidate& candidate : op.candidates) {
+        for (const PlanStep& step : candidate.steps) {
+          const auto* invocation = std::get_if<KernelInvocation>(&step);
+          if (invocation == nullptr) continue;
+          for (const auto& argument : invocation->artifact.arguments) {
+            const std::string& transform = argument.source.prepack;
+            if (transform.empty()) continue;
+            const auto slot = static_cast<std::size_t>(argument.source.index);
+            if (slot >= invocation->inputs.size()) {
+              return Status::Internal("kernel " + invocation->artifact.kernel_id + ": prepack argument '" +
+                                      argument.name + "' names input " + std::to_string(slot));
             }
-            const Tensor& host = found->second;
-            TensorDesc desc = plan.graph().FindValue(base)->tensor;
-            TensorDesc out_desc;
-            std::vector<std::uint8_t> out_bytes;
-            CUTRITON_RETURN_IF_ERROR(RunPrepack(
-                arg.source.prepack, desc,
-                static_cast<const std::uint8_t*>(host.buffer()->data()) + host.byte_offset(), &out_desc,
-                &out_bytes));
-            out_desc.device_type = DeviceType::kCUDA;
-            out_desc.device_id = plan.backend_options().device.id;
-            CUTRITON_RETURN_IF_ERROR(Upload(derived, out_desc, out_bytes.data()));
+            const std::string& base = invocation->inputs[slot];
+            const std::string derived = PrepackedName(base, transform);
+            if (constants_.count(derived) != 0) continue;
+            const auto host = plan.constants().find(base);
+            if (host == plan.constants().end()) {
+              return Status::InvalidArgument("prepack '" + transform + "' needs a constant, '" + base + "' is not one");
+            }
+            TensorDesc packed_desc;
+            std::vector<std::uint8_t> packed;
+            CUTRITON_RETURN_IF_ERROR(RunPrepack(transform, plan.graph().FindValue(base)->tensor,
+                                                HostBytes(host->second), &packed_desc, &packed));
+            CUTRITON_RETURN_IF_ERROR(Place(derived, std::move(packed_desc), packed.data()));
           }
         }
       }
@@ -380,8 +129,10 @@ class EngineState {
 
   std::once_flag constants_once_;
   Status constants_status_;
-  std::once_flag cache_once_;
-  Status cache_status_;
+  std::unordered_map<std::string, Tensor> constants_;
+  std::once_flag modules_once_;
+  Status modules_status_;
+  std::shared_ptr<CudaModuleCache> modules_;
 };
 
 Engine::Engine(ExecutablePlan plan) : state_(std::make_shared<EngineState>(std::move(plan))) {}
@@ -392,387 +143,415 @@ std::unique_ptr<ExecutionContext> Engine::CreateExecutionContext() const {
   return std::make_unique<ExecutionContext>(state_);
 }
 
-ExecutionContext::ExecutionContext(std::shared_ptr<EngineState> state) : state_(std::move(state)) {
+// ---- per-context session -----------------------------------------------------------
+
+struct ExecutionContext::Session {
+  // Shapes.
+  int profile{-1};
+  std::unordered_map<std::string, std::vector<int64_t>> input_shapes;
+  Graph resolved;
+  bool resolved_ok{false};
+
+  // Epochs (see the file comment) and what each stage was built at.
+  std::uint64_t layout{1}, binding{1}, choice{1};
+  std::pair<std::uint64_t, std::uint64_t> table_at{0, 0};
+  std::pair<std::uint64_t, std::uint64_t> selection_at{0, 0};
+  std::pair<std::uint64_t, std::uint64_t> kernels_at{0, 0};
+
+  std::unordered_map<std::string, Tensor> bound;    // graph inputs / outputs given by the caller
+  std::unordered_map<std::string, Tensor> tensors;  // everything a kernel may look up
+  std::shared_ptr<Buffer> workspace;
+  std::unordered_map<std::size_t, std::size_t> pins;
+  std::vector<std::size_t> chosen;
+  std::vector<std::vector<std::unique_ptr<OpKernel>>> kernels;
+  std::vector<char> timed;  // per op: profiled with events (has a kernel launch)
+
+  Profiler profiler;
+  bool pending{false};
+  CUstream stream{nullptr};
+  std::unique_ptr<runtime::DeviceSession> device;
+  std::unique_ptr<runtime::GraphCache> graphs;
+
+  const Graph& graph(const ExecutablePlan& plan) const { return resolved_ok ? resolved : plan.graph(); }
+  void ShapesChanged() {
+    ++layout;
+    bound.clear();
+    tensors.clear();
+  }
+};
+
+namespace {
+
+Status CheckBinding(const std::string& name, const TensorDesc& want, const Tensor& tensor) {
+  CUTRITON_RETURN_IF_ERROR(tensor.desc().Validate());
+  const std::string where = "binding '" + name + "': ";
+  if (!tensor.defined() || tensor.buffer()->empty()) return Status::InvalidArgument(where + "no buffer");
+  const TensorDesc& got = tensor.desc();
+  if (got.shape != want.shape || got.dtype != want.dtype || got.layout != want.layout) {
+    return Status::InvalidArgument(where + "shape, dtype or layout differs from the plan");
+  }
+  if (got.device_type != want.device_type || got.device_id != want.device_id ||
+      tensor.buffer()->device_type() != want.device_type || tensor.buffer()->device_id() != want.device_id) {
+    return Status::InvalidArgument(where + "not on the plan's device");
+  }
+  const std::size_t capacity = tensor.buffer()->size_bytes();
+  if (tensor.byte_offset() > capacity || want.ByteSize() > capacity - tensor.byte_offset()) {
+    return Status::InvalidArgument(where + "the buffer is smaller than the tensor");
+  }
+  return Status::OK();
+}
+
+bool OnlyViews(const ExecutionCandidate& candidate) {
+  return std::none_of(candidate.steps.begin(), candidate.steps.end(),
+                      [](const PlanStep& s) { return std::holds_alternative<KernelInvocation>(s); });
+}
+
+}  // namespace
+
+ExecutionContext::ExecutionContext(std::shared_ptr<EngineState> state)
+    : state_(std::move(state)), session_(std::make_unique<Session>()) {
+  // A plan with a single profile starts on it, at its opt shapes.
   if (state_ != nullptr && state_->plan.profile_plans().size() == 1) {
-    selected_profile_ = 0;
-    const ProfilePlan& pp = state_->plan.profile_plans().front();
-    resolved_graph_ = pp.opt_graph;
-    shapes_resolved_ = true;
-    for (const auto& entry : pp.profile.inputs) input_shapes_[entry.first] = entry.second.opt;
+    const ProfilePlan& only = state_->plan.profile_plans().front();
+    session_->profile = 0;
+    session_->resolved = only.opt_graph;
+    session_->resolved_ok = true;
+    for (const auto& [input, range] : only.profile.inputs) session_->input_shapes[input] = range.opt;
   }
 }
 
 ExecutionContext::~ExecutionContext() {
   (void)Synchronize();
-  DestroyCudaState(static_cast<CudaState*>(cuda_state_));
+  if (session_->device != nullptr) (void)session_->device->MakeCurrent();
+  session_->graphs.reset();
+  session_->kernels.clear();
+  session_->device.reset();
 }
 
-const Graph& ExecutionContext::ActiveGraph() const {
-  return shapes_resolved_ ? resolved_graph_ : state_->plan.graph();
+bool ExecutionContext::run_pending() const { return session_->pending; }
+const Profiler& ExecutionContext::profiler() const { return session_->profiler; }
+const std::unordered_map<std::string, Tensor>& ExecutionContext::tensors() const { return session_->tensors; }
+const std::vector<std::size_t>& ExecutionContext::selected_candidates() const { return session_->chosen; }
+
+std::size_t ExecutionContext::cached_cuda_graph_count() const {
+  return session_->graphs == nullptr ? 0 : session_->graphs->size();
 }
+
+std::size_t ExecutionContext::loaded_cuda_module_count() const {
+  return state_ == nullptr ? 0 : state_->module_count();
+}
+
+const Graph& ExecutionContext::ActiveGraph() const { return session_->graph(state_->plan); }
 
 const MemoryPlan& ExecutionContext::ActiveMemoryPlan() const {
-  if (selected_profile_ >= 0) {
-    return state_->plan.profile_plans().at(static_cast<std::size_t>(selected_profile_)).max_memory_plan;
-  }
-  return state_->plan.memory_plan();
+  const int p = session_->profile;
+  return p >= 0 ? state_->plan.profile_plans().at(static_cast<std::size_t>(p)).max_memory_plan
+                : state_->plan.memory_plan();
 }
 
-Status ExecutionContext::BindInput(const std::string& name, Tensor tensor) {
-  if (state_ == nullptr) return Status::InvalidArgument("ExecutionContext has no engine state");
-  if (run_pending_) return Status::RuntimeError("cannot bind a tensor while a run is pending");
-  if (!state_->plan.profile_plans().empty() && !shapes_resolved_) {
-    return Status::RuntimeError("ResolveShapes must be called before binding");
+// ---- binding and shapes -------------------------------------------------------------
+
+namespace {
+
+Status CheckBoundary(bool pending, bool needs_resolve, const Graph& graph, const std::vector<std::string>& boundary,
+                     const char* what, const std::string& name, const Tensor& tensor) {
+  if (pending) return Status::RuntimeError("cannot bind '" + name + "' while a run is pending");
+  if (needs_resolve) return Status::RuntimeError("call ResolveShapes before binding '" + name + "'");
+  if (std::find(boundary.begin(), boundary.end(), name) == boundary.end()) {
+    return Status::NotFound("'" + name + "' is not a graph " + what);
   }
-  const Graph& graph = ActiveGraph();
-  if (!Contains(graph.inputs(), name)) return Status::NotFound("name is not a graph input: " + name);
   const ValueDesc* value = graph.FindValue(name);
-  if (value == nullptr) return Status::NotFound("graph input description is missing: " + name);
-  CUTRITON_RETURN_IF_ERROR(ValidateBoundTensor(name, value->tensor, tensor));
-  tensors_[name] = std::move(tensor);
-  tensors_prepared_ = false;
+  if (value == nullptr) return Status::NotFound("graph " + std::string(what) + " '" + name + "' has no description");
+  return CheckBinding(name, value->tensor, tensor);
+}
+
+}  // namespace
+
+Status ExecutionContext::BindInput(const std::string& name, Tensor tensor) {
+  if (state_ == nullptr) return Status::InvalidArgument("BindInput: the context has no engine");
+  const bool needs_resolve = !state_->plan.profile_plans().empty() && !session_->resolved_ok;
+  CUTRITON_RETURN_IF_ERROR(
+      CheckBoundary(session_->pending, needs_resolve, ActiveGraph(), ActiveGraph().inputs(), "input", name, tensor));
+  session_->bound[name] = std::move(tensor);
+  ++session_->binding;
   return Status::OK();
 }
 
 Status ExecutionContext::BindOutput(const std::string& name, Tensor tensor) {
-  if (state_ == nullptr) return Status::InvalidArgument("ExecutionContext has no engine state");
-  if (run_pending_) return Status::RuntimeError("cannot bind a tensor while a run is pending");
-  if (!state_->plan.profile_plans().empty() && !shapes_resolved_) {
-    return Status::RuntimeError("ResolveShapes must be called before binding");
-  }
-  const Graph& graph = ActiveGraph();
-  if (!Contains(graph.outputs(), name)) return Status::NotFound("name is not a graph output: " + name);
-  const ValueDesc* value = graph.FindValue(name);
-  if (value == nullptr) return Status::NotFound("graph output description is missing: " + name);
-  CUTRITON_RETURN_IF_ERROR(ValidateBoundTensor(name, value->tensor, tensor));
-  tensors_[name] = std::move(tensor);
-  tensors_prepared_ = false;
+  if (state_ == nullptr) return Status::InvalidArgument("BindOutput: the context has no engine");
+  const bool needs_resolve = !state_->plan.profile_plans().empty() && !session_->resolved_ok;
+  CUTRITON_RETURN_IF_ERROR(
+      CheckBoundary(session_->pending, needs_resolve, ActiveGraph(), ActiveGraph().outputs(), "output", name, tensor));
+  session_->bound[name] = std::move(tensor);
+  ++session_->binding;
   return Status::OK();
 }
 
 Status ExecutionContext::SelectShapeProfile(const std::string& name) {
-  if (run_pending_) return Status::RuntimeError("cannot change the profile while a run is pending");
-  const auto& profiles = state_->plan.profile_plans();
-  const auto found = std::find_if(profiles.begin(), profiles.end(),
-                                  [&](const ProfilePlan& p) { return p.profile.name == name; });
-  if (found == profiles.end()) return Status::NotFound("ShapeProfile is not defined: " + name);
-  selected_profile_ = static_cast<int>(found - profiles.begin());
-  input_shapes_.clear();
-  for (const auto& entry : found->profile.inputs) input_shapes_[entry.first] = entry.second.opt;
-  resolved_graph_ = found->opt_graph;
-  shapes_resolved_ = true;
-  tensors_.clear();
-  workspace_.reset();
-  tensors_prepared_ = false;
-  kernels_.clear();
-  kernels_prepared_ = false;
-  tuning_prepared_ = false;
-  InvalidateCudaGraph();
+  Session& s = *session_;
+  if (s.pending) return Status::RuntimeError("cannot switch shape profiles while a run is pending");
+  const auto& plans = state_->plan.profile_plans();
+  const auto it = std::find_if(plans.begin(), plans.end(), [&](const ProfilePlan& p) { return p.profile.name == name; });
+  if (it == plans.end()) return Status::NotFound("no shape profile named '" + name + "'");
+  s.profile = static_cast<int>(it - plans.begin());
+  s.input_shapes.clear();
+  for (const auto& [input, range] : it->profile.inputs) s.input_shapes[input] = range.opt;
+  s.resolved = it->opt_graph;
+  s.resolved_ok = true;
+  s.ShapesChanged();
+  s.workspace.reset();
+  // Graphs captured for the old profile reference its workspace.
+  if (s.graphs != nullptr) {
+    if (s.device != nullptr) (void)s.device->MakeCurrent();
+    s.graphs->Clear();
+  }
   return Status::OK();
 }
 
 Status ExecutionContext::SetInputShape(const std::string& name, std::vector<int64_t> shape) {
-  if (run_pending_) return Status::RuntimeError("cannot change a shape while a run is pending");
-  if (selected_profile_ < 0) return Status::RuntimeError("select a ShapeProfile before setting shapes");
-  const ShapeProfile& profile =
-      state_->plan.profile_plans().at(static_cast<std::size_t>(selected_profile_)).profile;
+  Session& s = *session_;
+  if (s.pending) return Status::RuntimeError("cannot change input shapes while a run is pending");
+  if (s.profile < 0) return Status::RuntimeError("SetInputShape needs a selected shape profile");
+  const ShapeProfile& profile = state_->plan.profile_plans().at(static_cast<std::size_t>(s.profile)).profile;
   const auto range = profile.inputs.find(name);
-  if (range == profile.inputs.end()) return Status::NotFound("name is not a profiled graph input: " + name);
-  if (shape.size() != range->second.min.size()) {
-    return Status::ShapeError("input shape rank does not match the profile: " + name);
-  }
-  for (std::size_t a = 0; a < shape.size(); ++a) {
-    if (shape[a] < range->second.min[a] || shape[a] > range->second.max[a]) {
-      return Status::ShapeError("input shape is outside the profile range: " + name);
+  if (range == profile.inputs.end()) return Status::NotFound("'" + name + "' is not an input of the shape profile");
+  const ShapeRange& r = range->second;
+  if (shape.size() != r.min.size()) return Status::ShapeError("'" + name + "': rank differs from the profile");
+  for (std::size_t axis = 0; axis < shape.size(); ++axis) {
+    if (shape[axis] < r.min[axis] || shape[axis] > r.max[axis]) {
+      return Status::ShapeError("'" + name + "': axis " + std::to_string(axis) + " is outside the profile's range");
     }
   }
-  input_shapes_[name] = std::move(shape);
-  shapes_resolved_ = false;
-  tensors_.clear();
-  tensors_prepared_ = false;
-  kernels_.clear();
-  kernels_prepared_ = false;
-  tuning_prepared_ = false;
+  s.input_shapes[name] = std::move(shape);
+  s.resolved_ok = false;
+  s.ShapesChanged();
   return Status::OK();
 }
 
 Status ExecutionContext::ResolveShapes() {
-  if (selected_profile_ < 0) return Status::RuntimeError("select a ShapeProfile before resolving shapes");
-  const ProfilePlan& pp = state_->plan.profile_plans().at(static_cast<std::size_t>(selected_profile_));
-  Graph graph = pp.opt_graph;
-  for (const auto& input : graph.inputs()) {
-    const auto shape = input_shapes_.find(input);
-    if (shape == input_shapes_.end()) return Status::InvalidArgument("input shape is not set: " + input);
-    TensorDesc desc = graph.FindValue(input)->tensor;
-    desc.shape = shape->second;
-    CUTRITON_RETURN_IF_ERROR(graph.SetValueDesc(input, std::move(desc)));
+  Session& s = *session_;
+  if (s.profile < 0) return Status::RuntimeError("ResolveShapes needs a selected shape profile");
+  Graph graph = state_->plan.profile_plans().at(static_cast<std::size_t>(s.profile)).opt_graph;
+  for (const std::string& input : graph.inputs()) {
+    const auto shape = s.input_shapes.find(input);
+    if (shape == s.input_shapes.end()) return Status::InvalidArgument("no shape set for input '" + input + "'");
+    graph.MutableValue(input)->tensor.shape = shape->second;
   }
   CUTRITON_RETURN_IF_ERROR(CreateShapeInferencePass()->Run(&graph));
-  resolved_graph_ = std::move(graph);
-  shapes_resolved_ = true;
+  s.resolved = std::move(graph);
+  s.resolved_ok = true;
+  ++s.layout;
   return Status::OK();
 }
 
 const TensorDesc* ExecutionContext::GetResolvedTensorDesc(const std::string& name) const {
-  if (!shapes_resolved_) return nullptr;
-  const ValueDesc* v = resolved_graph_.FindValue(name);
-  return v == nullptr ? nullptr : &v->tensor;
-}
-
-std::size_t ExecutionContext::cached_cuda_graph_count() const {
-  const auto* s = static_cast<const CudaState*>(cuda_state_);
-  return s == nullptr ? 0 : s->graphs.size();
-}
-
-std::size_t ExecutionContext::loaded_cuda_module_count() const {
-  return state_ == nullptr ? 0 : LoadedModuleCount(state_->module_cache);
-}
-
-Status ExecutionContext::PrepareTensors() {
-  if (tensors_prepared_) return Status::OK();
-  if (state_ == nullptr) return Status::InvalidArgument("ExecutionContext has no engine state");
-  CUTRITON_RETURN_IF_ERROR(state_->InitializeConstants());
-  for (const auto& entry : state_->device_constants) tensors_[entry.first] = entry.second;
-  const MemoryPlan& plan = ActiveMemoryPlan();
-  const BackendOptions& options = state_->plan.backend_options();
-  if (plan.workspace_size_bytes != 0 &&
-      (workspace_ == nullptr || workspace_->size_bytes() < plan.workspace_size_bytes)) {
-    if (options.device.type == DeviceType::kCUDA) {
-      CUTRITON_RETURN_IF_ERROR(Buffer::AllocateCuda(plan.workspace_size_bytes, options.device.id, &workspace_));
-    } else {
-      workspace_ = Buffer::AllocateHost(plan.workspace_size_bytes);
-    }
-  }
-  const Graph& graph = ActiveGraph();
-  for (const auto& a : plan.allocations) {
-    const ValueDesc* value = graph.FindValue(a.value_name);
-    if (value == nullptr) {
-      // Candidate temporary: shaped like its `like_value`.
-      const ValueDesc* like = nullptr;
-      for (const auto& op : state_->plan.ops()) {
-        for (const auto& c : op.candidates) {
-          for (const auto& t : c.temporaries) {
-            if (t.name == a.value_name) like = graph.FindValue(t.like_value);
-          }
-        }
-        if (like != nullptr) break;
-      }
-      if (like == nullptr) return Status::Internal("allocation references an unknown value: " + a.value_name);
-      tensors_[a.value_name] = Tensor(like->tensor, workspace_, a.offset);
-      continue;
-    }
-    if (!a.alias_of.empty()) {
-      const auto source = tensors_.find(a.alias_of);
-      if (source == tensors_.end()) return Status::Internal("alias source tensor is missing: " + a.alias_of);
-      if (value->tensor.ByteSize() != source->second.desc().ByteSize()) {
-        return Status::ShapeError("alias changes the byte size: " + a.value_name);
-      }
-      tensors_[a.value_name] = Tensor(value->tensor, source->second.buffer(), source->second.byte_offset());
-      continue;
-    }
-    if (workspace_ == nullptr || a.offset > workspace_->size_bytes() ||
-        a.size_bytes > workspace_->size_bytes() - a.offset) {
-      return Status::Internal("allocation exceeds the workspace: " + a.value_name);
-    }
-    tensors_[a.value_name] = Tensor(value->tensor, workspace_, a.offset);
-  }
-  tensors_prepared_ = true;
-  return Status::OK();
-}
-
-Status ExecutionContext::PrepareKernels() {
-  if (kernels_prepared_) return Status::OK();
-  if (state_ == nullptr) return Status::InvalidArgument("ExecutionContext has no engine state");
-  CUTRITON_RETURN_IF_ERROR(RegisterBuiltinBackends());
-  CUTRITON_RETURN_IF_ERROR(state_->InitializeModuleCache());
-  const auto& ops = state_->plan.ops();
-  if (selected_candidates_.size() != ops.size()) return Status::Internal("tuning selections are not prepared");
-  kernels_.clear();
-  for (std::size_t i = 0; i < ops.size(); ++i) {
-    const PlanOp& op = ops[i];
-    auto backend = KernelRegistry::Global().GetBackend(op.backend_name);
-    if (backend == nullptr) return Status::NotFound("backend is not registered: " + op.backend_name);
-    const Node& node = ActiveGraph().nodes().at(static_cast<std::size_t>(op.node_id));
-    if (selected_candidates_[i] >= op.candidates.size()) {
-      return Status::Internal("selected execution candidate is out of range");
-    }
-    const ExecutionCandidate& candidate = op.candidates[selected_candidates_[i]];
-    std::vector<std::unique_ptr<OpKernel>> group;
-    for (const auto& step : candidate.steps) {
-      std::unique_ptr<OpKernel> kernel;
-      if (const auto* inv = std::get_if<KernelInvocation>(&step)) {
-        CUTRITON_RETURN_IF_ERROR(CreateInvocationKernel(*inv, state_->plan.backend_options().device.id,
-                                                        state_->module_cache, &kernel));
-      } else {
-        CUTRITON_RETURN_IF_ERROR(backend->CreateKernel(node, ActiveGraph(), state_->plan.backend_options(), &kernel));
-      }
-      if (kernel == nullptr) return Status::Internal("backend returned a null OpKernel");
-      group.push_back(std::move(kernel));
-    }
-    if (group.empty()) {
-      std::unique_ptr<OpKernel> kernel;
-      CUTRITON_RETURN_IF_ERROR(backend->CreateKernel(node, ActiveGraph(), state_->plan.backend_options(), &kernel));
-      if (kernel == nullptr) return Status::Internal("backend returned a null OpKernel");
-      group.push_back(std::move(kernel));
-    }
-    kernels_.push_back(std::move(group));
-  }
-  kernels_prepared_ = true;
-  return Status::OK();
-}
-
-Status ExecutionContext::PrepareTuning() {
-  if (tuning_prepared_) return Status::OK();
-  const auto& ops = state_->plan.ops();
-  selected_candidates_.clear();
-  for (const auto& op : ops) selected_candidates_.push_back(op.selected_candidate);
-  for (const auto& pin : pinned_candidates_) selected_candidates_[pin.first] = pin.second;
-  const TuningConfig& config = state_->plan.tuning_config();
-  if (state_->plan.backend_options().device.type != DeviceType::kCUDA || config.mode == TuningMode::kDisabled) {
-    tuning_prepared_ = true;
-    return Status::OK();
-  }
-  CUTRITON_RETURN_IF_ERROR(state_->InitializeModuleCache());
-  const auto& api = drv::Get();
-  const int device_id = state_->plan.backend_options().device.id;
-  for (std::size_t i = 0; i < ops.size(); ++i) {
-    const PlanOp& op = ops[i];
-    if (op.candidates.size() < 2 || pinned_candidates_.count(i) != 0) continue;
-    const Node& node = ActiveGraph().nodes().at(static_cast<std::size_t>(op.node_id));
-    const std::string key = TuningKey(op, node, ActiveGraph(), device_id);
-    const std::filesystem::path cache_file = std::filesystem::path(config.cache_dir) / (key + ".json");
-    if (config.mode != TuningMode::kForceRetune) {
-      if (const auto cached = ReadTuningChoice(cache_file)) {
-        if (const auto index = CandidateIndex(op, *cached)) {
-          selected_candidates_[i] = *index;
-          continue;
-        }
-      }
-      if (config.mode == TuningMode::kUseCache && selected_profile_ >= 0) {
-        const Graph& opt = state_->plan.profile_plans().at(static_cast<std::size_t>(selected_profile_)).opt_graph;
-        const std::string opt_key = TuningKey(op, opt.nodes().at(static_cast<std::size_t>(op.node_id)), opt, device_id);
-        if (const auto cached = ReadTuningChoice(std::filesystem::path(config.cache_dir) / (opt_key + ".json"))) {
-          if (const auto index = CandidateIndex(op, *cached)) {
-            selected_candidates_[i] = *index;
-            continue;
-          }
-        }
-      }
-    }
-    if (config.mode == TuningMode::kUseCache) continue;
-
-    CUstream stream{};
-    CUevent start{}, end{};
-    CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuStreamCreate(&stream, CU_STREAM_NON_BLOCKING), "cuStreamCreate"));
-    CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuEventCreate(&start, CU_EVENT_DEFAULT), "cuEventCreate"));
-    CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuEventCreate(&end, CU_EVENT_DEFAULT), "cuEventCreate"));
-    struct Cleanup {
-      CUstream s; CUevent a, b;
-      ~Cleanup() {
-        const auto& d = drv::Get();
-        d.cuEventDestroy(a);
-        d.cuEventDestroy(b);
-        d.cuStreamDestroy(s);
-      }
-    } cleanup{stream, start, end};
-    auto* cuda = static_cast<CudaState*>(cuda_state_);
-    void* scratch = cuda == nullptr ? nullptr : reinterpret_cast<void*>(cuda->error_device);
-    double best_ms = std::numeric_limits<double>::infinity();
-    std::size_t best = op.selected_candidate;
-    std::vector<float> reference;
-    // The default candidate runs first and is the numerical reference (it is
-    // always eligible); intermediate inputs may hold anything during tuning,
-    // so elements where it is not finite are not compared.
-    std::vector<std::size_t> order{op.selected_candidate};
-    for (std::size_t c = 0; c < op.candidates.size(); ++c) {
-      if (c != op.selected_candidate) order.push_back(c);
-    }
-    for (const std::size_t c : order) {
-      std::vector<std::unique_ptr<OpKernel>> kernels;
-      for (const auto& step : op.candidates[c].steps) {
-        const auto* inv = std::get_if<KernelInvocation>(&step);
-        if (inv == nullptr) continue;
-        std::unique_ptr<OpKernel> kernel;
-        CUTRITON_RETURN_IF_ERROR(CreateInvocationKernel(*inv, device_id, state_->module_cache, &kernel));
-        kernels.push_back(std::move(kernel));
-      }
-      if (kernels.empty()) continue;
-      KernelContext ctx{&node, &tensors_, stream, nullptr, scratch};
-      for (int w = 0; w < config.warmup_iterations; ++w) {
-        for (auto& k : kernels) CUTRITON_RETURN_IF_ERROR(k->Compute(&ctx));
-      }
-      CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuStreamSynchronize(stream), "cuStreamSynchronize"));
-      std::vector<float> produced;
-      CUTRITON_RETURN_IF_ERROR(CopyAsFloat(tensors_.at(op.outputs.front()), &produced));
-      if (reference.empty()) {
-        reference = produced;
-      } else {
-        // Numerically different candidates are never chosen.
-        const float rel = tensors_.at(op.outputs.front()).desc().dtype == DataType::kFloat16 ? 1e-2f : 1e-4f;
-        bool same = true;
-        for (std::size_t e = 0; e < produced.size() && same; ++e) {
-          if (!std::isfinite(reference[e])) continue;
-          const float tol = rel + rel * std::fabs(reference[e]);
-          same = std::isfinite(produced[e]) && std::fabs(produced[e] - reference[e]) <= tol;
-        }
-        if (!same) continue;
-      }
-      std::vector<float> samples;
-      for (int r = 0; r < config.measurement_iterations; ++r) {
-        CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuEventRecord(start, stream), "cuEventRecord"));
-        for (auto& k : kernels) CUTRITON_RETURN_IF_ERROR(k->Compute(&ctx));
-        CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuEventRecord(end, stream), "cuEventRecord"));
-        CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuEventSynchronize(end), "cuEventSynchronize"));
-        float ms = 0.0f;
-        CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuEventElapsedTime(&ms, start, end), "cuEventElapsedTime"));
-        samples.push_back(ms);
-      }
-      if (samples.empty()) continue;
-      std::sort(samples.begin(), samples.end());
-      const double median = samples[samples.size() / 2];
-      if (median < best_ms) {
-        best_ms = median;
-        best = c;
-      }
-    }
-    if (!std::isfinite(best_ms)) return Status::RuntimeError("no numerically valid tuning candidate for " + op.node_name);
-    selected_candidates_[i] = best;
-    CUTRITON_RETURN_IF_ERROR(WriteTuningChoice(cache_file, key, op.candidates[best].candidate_id, best_ms));
-  }
-  tuning_prepared_ = true;
-  return Status::OK();
+  if (!session_->resolved_ok) return nullptr;
+  const ValueDesc* value = session_->resolved.FindValue(name);
+  return value == nullptr ? nullptr : &value->tensor;
 }
 
 Status ExecutionContext::SelectCandidate(std::size_t op, std::size_t candidate) {
-  if (run_pending_) return Status::RuntimeError("cannot select a candidate while a run is pending");
+  if (session_->pending) return Status::RuntimeError("cannot pin a candidate while a run is pending");
   const auto& ops = state_->plan.ops();
-  if (op >= ops.size()) return Status::InvalidArgument("plan op index is out of range");
-  if (candidate >= ops[op].candidates.size()) return Status::InvalidArgument("candidate index is out of range");
-  pinned_candidates_[op] = candidate;
-  tuning_prepared_ = false;
-  kernels_prepared_ = false;
-  kernels_.clear();
+  if (op >= ops.size()) return Status::InvalidArgument("SelectCandidate: op " + std::to_string(op) + " does not exist");
+  if (candidate >= ops[op].candidates.size()) {
+    return Status::InvalidArgument("SelectCandidate: op " + ops[op].node_name + " has no candidate " +
+                                   std::to_string(candidate));
+  }
+  session_->pins[op] = candidate;
+  ++session_->choice;
+  return Status::OK();
+}
+
+// ---- preparation stages ---------------------------------------------------------------
+
+Status ExecutionContext::PrepareTensors() {
+  Session& s = *session_;
+  if (s.table_at == std::make_pair(s.layout, s.binding)) return Status::OK();
+  if (state_ == nullptr) return Status::InvalidArgument("the context has no engine");
+  const std::unordered_map<std::string, Tensor>* constants = nullptr;
+  CUTRITON_RETURN_IF_ERROR(state_->Constants(&constants));
+  const MemoryPlan& memory = ActiveMemoryPlan();
+  const Graph& graph = ActiveGraph();
+  const Device& device = state_->plan.backend_options().device;
+  if (memory.workspace_size_bytes > 0 && (s.workspace == nullptr || s.workspace->size_bytes() < memory.workspace_size_bytes)) {
+    if (device.type == DeviceType::kCUDA) {
+      CUTRITON_RETURN_IF_ERROR(Buffer::AllocateCuda(memory.workspace_size_bytes, device.id, &s.workspace));
+    } else {
+      s.workspace = Buffer::AllocateHost(memory.workspace_size_bytes);
+    }
+  }
+  // Temporaries of unfused candidates are shaped like another value.
+  std::unordered_map<std::string, std::string> temporary_like;
+  for (const PlanOp& op : state_->plan.ops()) {
+    for (const ExecutionCandidate& c : op.candidates) {
+      for (const CandidateTemporary& t : c.temporaries) temporary_like.emplace(t.name, t.like_value);
+    }
+  }
+  std::unordered_map<std::string, Tensor> table = *constants;
+  for (const auto& [name, tensor] : s.bound) table[name] = tensor;
+  for (const Allocation& a : memory.allocations) {
+    const ValueDesc* value = graph.FindValue(a.value_name);
+    if (value == nullptr) {
+      const auto like = temporary_like.find(a.value_name);
+      const ValueDesc* shape = like == temporary_like.end() ? nullptr : graph.FindValue(like->second);
+      if (shape == nullptr) return Status::Internal("workspace entry '" + a.value_name + "' names no value");
+      table[a.value_name] = Tensor(shape->tensor, s.workspace, a.offset);
+      continue;
+    }
+    if (!a.alias_of.empty()) {
+      // Allocations come in definition order, so a view's source (planned,
+      // constant or bound) is already in the table.
+      const auto source = table.find(a.alias_of);
+      if (source == table.end()) return Status::Internal("view '" + a.value_name + "' has no source tensor");
+      if (source->second.desc().ByteSize() != value->tensor.ByteSize()) {
+        return Status::ShapeError("view '" + a.value_name + "' would change the byte size of '" + a.alias_of + "'");
+      }
+      table[a.value_name] = Tensor(value->tensor, source->second.buffer(), source->second.byte_offset());
+      continue;
+    }
+    if (s.workspace == nullptr || a.offset > s.workspace->size_bytes() ||
+        a.size_bytes > s.workspace->size_bytes() - a.offset) {
+      return Status::Internal("workspace entry '" + a.value_name + "' lies outside the workspace");
+    }
+    table[a.value_name] = Tensor(value->tensor, s.workspace, a.offset);
+  }
+  s.tensors = std::move(table);
+  s.table_at = {s.layout, s.binding};
   return Status::OK();
 }
 
 Status ExecutionContext::ValidateBindings() const {
+  const Session& s = *session_;
   const Graph& graph = ActiveGraph();
-  for (const auto& name : graph.inputs()) {
-    if (tensors_.count(name) == 0) return Status::InvalidArgument("graph input is not bound: " + name);
+  for (const std::string& name : graph.inputs()) {
+    if (s.bound.count(name) == 0) return Status::InvalidArgument("graph input '" + name + "' is not bound");
   }
-  for (const auto& name : graph.outputs()) {
-    if (tensors_.count(name) == 0) return Status::InvalidArgument("graph output is not bound: " + name);
+  for (const std::string& name : graph.outputs()) {
+    if (s.bound.count(name) == 0) return Status::InvalidArgument("graph output '" + name + "' is not bound");
   }
-  for (const auto& node : graph.nodes()) {
-    for (const auto& name : node.inputs()) {
-      if (tensors_.count(name) == 0) return Status::InvalidArgument("node input tensor is missing: " + name);
-    }
-    for (const auto& name : node.outputs()) {
-      if (tensors_.count(name) == 0) return Status::InvalidArgument("node output tensor is missing: " + name);
+  for (const Node& node : graph.nodes()) {
+    for (const auto* names : {&node.inputs(), &node.outputs()}) {
+      for (const std::string& name : *names) {
+        if (s.tensors.count(name) == 0) {
+          return Status::InvalidArgument("node '" + node.name() + "' uses '" + name + "', which has no tensor");
+        }
+      }
     }
   }
   return Status::OK();
 }
+
+Status ExecutionContext::PrepareTuning() {
+  Session& s = *session_;
+  if (s.selection_at == std::make_pair(s.layout, s.choice)) return Status::OK();
+  const auto& ops = state_->plan.ops();
+  std::vector<std::size_t> chosen(ops.size());
+  for (std::size_t i = 0; i < ops.size(); ++i) {
+    const auto pin = s.pins.find(i);
+    chosen[i] = pin != s.pins.end() ? pin->second : ops[i].selected_candidate;
+  }
+  const TuningConfig& config = state_->plan.tuning_config();
+  if (state_->on_cuda() && config.mode != TuningMode::kDisabled) {
+    std::shared_ptr<CudaModuleCache> modules;
+    CUTRITON_RETURN_IF_ERROR(state_->Modules(&modules));
+    const int device_id = state_->device_id();
+    const Graph& graph = ActiveGraph();
+    for (std::size_t i = 0; i < ops.size(); ++i) {
+      const PlanOp& op = ops[i];
+      if (op.candidates.size() < 2 || s.pins.count(i) != 0) continue;
+      const Node& node = graph.nodes().at(static_cast<std::size_t>(op.node_id));
+      const std::string key = runtime::TuningFingerprint(op, node, graph, device_id);
+      std::optional<std::string> cached;
+      if (config.mode != TuningMode::kForceRetune) {
+        cached = runtime::LoadTuningChoice(config.cache_dir, key);
+        // UseCache also accepts a choice recorded at the profile's opt shapes.
+        if (!cached && config.mode == TuningMode::kUseCache && s.profile >= 0) {
+          const Graph& opt = state_->plan.profile_plans().at(static_cast<std::size_t>(s.profile)).opt_graph;
+          cached = runtime::LoadTuningChoice(
+              config.cache_dir,
+              runtime::TuningFingerprint(op, opt.nodes().at(static_cast<std::size_t>(op.node_id)), opt, device_id));
+        }
+      }
+      if (cached) {
+        const auto match = std::find_if(op.candidates.begin(), op.candidates.end(),
+                                        [&](const ExecutionCandidate& c) { return c.candidate_id == *cached; });
+        if (match != op.candidates.end()) {
+          chosen[i] = static_cast<std::size_t>(match - op.candidates.begin());
+          continue;
+        }
+      }
+      if (config.mode == TuningMode::kUseCache) continue;
+      runtime::TuningTarget target;
+      target.op = &op;
+      target.node = &node;
+      target.device_id = device_id;
+      target.tensors = &s.tensors;
+      target.error_word = s.device == nullptr ? nullptr : s.device->error_word_device();
+      target.modules = modules;
+      std::vector<double> medians;
+      CUTRITON_RETURN_IF_ERROR(runtime::TuneCandidates(target, config, &chosen[i], &medians));
+      CUTRITON_RETURN_IF_ERROR(runtime::StoreTuningChoice(config.cache_dir, key, op, chosen[i], medians));
+    }
+  }
+  s.chosen = std::move(chosen);
+  s.selection_at = {s.layout, s.choice};
+  return Status::OK();
+}
+
+Status ExecutionContext::PrepareKernels() {
+  Session& s = *session_;
+  if (s.kernels_at == std::make_pair(s.layout, s.choice) && !s.kernels.empty()) return Status::OK();
+  if (state_ == nullptr) return Status::InvalidArgument("the context has no engine");
+  CUTRITON_RETURN_IF_ERROR(RegisterBuiltinBackends());
+  std::shared_ptr<CudaModuleCache> modules;
+  CUTRITON_RETURN_IF_ERROR(state_->Modules(&modules));
+  const auto& ops = state_->plan.ops();
+  if (s.chosen.size() != ops.size()) return Status::Internal("candidate selection has not run");
+  const Graph& graph = ActiveGraph();
+  const BackendOptions& options = state_->plan.backend_options();
+  std::vector<std::vector<std::unique_ptr<OpKernel>>> built(ops.size());
+  std::vector<char> timed(ops.size(), 0);
+  for (std::size_t i = 0; i < ops.size(); ++i) {
+    const PlanOp& op = ops[i];
+    const std::shared_ptr<Backend> backend = KernelRegistry::Global().GetBackend(op.backend_name);
+    if (backend == nullptr) return Status::NotFound("backend '" + op.backend_name + "' is not registered");
+    if (s.chosen[i] >= op.candidates.size()) return Status::Internal("op " + op.node_name + ": candidate out of range");
+    const ExecutionCandidate& candidate = op.candidates[s.chosen[i]];
+    const Node& node = graph.nodes().at(static_cast<std::size_t>(op.node_id));
+    const auto from_backend = [&]() -> Status {
+      std::unique_ptr<OpKernel> kernel;
+      CUTRITON_RETURN_IF_ERROR(backend->CreateKernel(node, graph, options, &kernel));
+      if (kernel == nullptr) return Status::Internal("backend '" + op.backend_name + "' made no kernel for " + op.node_name);
+      built[i].push_back(std::move(kernel));
+      return Status::OK();
+    };
+    for (const PlanStep& step : candidate.steps) {
+      if (const auto* invocation = std::get_if<KernelInvocation>(&step)) {
+        std::unique_ptr<OpKernel> kernel;
+        CUTRITON_RETURN_IF_ERROR(CreateInvocationKernel(*invocation, options.device.id, modules, &kernel));
+        built[i].push_back(std::move(kernel));
+      } else {
+        CUTRITON_RETURN_IF_ERROR(from_backend());
+      }
+    }
+    // A candidate without steps (CPU / plugin backends) runs the backend's kernel.
+    if (candidate.steps.empty()) CUTRITON_RETURN_IF_ERROR(from_backend());
+    timed[i] = !OnlyViews(candidate) && !candidate.steps.empty();
+  }
+  s.kernels = std::move(built);
+  s.timed = std::move(timed);
+  s.kernels_at = {s.layout, s.choice};
+  return Status::OK();
+}
+
+void ExecutionContext::InvalidateCudaGraph() {
+  if (session_->graphs == nullptr) return;
+  if (session_->device != nullptr) (void)session_->device->MakeCurrent();
+  session_->graphs->Clear();
+}
+
+// ---- running ----------------------------------------------------------------------------
 
 Status ExecutionContext::Run() {
   CUTRITON_RETURN_IF_ERROR(RunAsync(nullptr));
@@ -780,157 +559,108 @@ Status ExecutionContext::Run() {
 }
 
 Status ExecutionContext::RunAsync(void* stream) {
-  if (run_pending_) return Status::RuntimeError("a run is already pending");
+  Session& s = *session_;
+  if (s.pending) return Status::RuntimeError("RunAsync: the previous run has not been synchronised");
   CUTRITON_RETURN_IF_ERROR(PrepareTensors());
   CUTRITON_RETURN_IF_ERROR(ValidateBindings());
-  const bool use_cuda = state_->plan.backend_options().device.type == DeviceType::kCUDA;
-  if (use_cuda && cuda_state_ == nullptr) {
-    auto* created = new CudaState();
-    const Status status = InitializeCudaState(created, state_->plan.backend_options().device.id,
-                                              state_->plan.ops().size(), state_->plan.enable_profiling());
-    if (!status.ok()) {
-      DestroyCudaState(created);
-      return status;
-    }
-    cuda_state_ = created;
+  const ExecutablePlan& plan = state_->plan;
+  if (state_->on_cuda() && s.device == nullptr) {
+    CUTRITON_RETURN_IF_ERROR(
+        runtime::DeviceSession::Open(state_->device_id(), plan.ops().size(), plan.enable_profiling(), &s.device));
+    s.graphs = std::make_unique<runtime::GraphCache>(plan.cuda_graph_cache_capacity());
   }
   CUTRITON_RETURN_IF_ERROR(PrepareTuning());
   CUTRITON_RETURN_IF_ERROR(PrepareKernels());
+  const Graph& graph = ActiveGraph();
 
-  if (!use_cuda) {
-    profiler_.Clear();
-    for (std::size_t i = 0; i < kernels_.size(); ++i) {
-      const PlanOp& op = state_->plan.ops()[i];
-      const Node& node = ActiveGraph().nodes().at(static_cast<std::size_t>(op.node_id));
-      KernelContext ctx{&node, &tensors_, stream, state_->plan.enable_profiling() ? &profiler_ : nullptr, nullptr};
-      for (auto& kernel : kernels_[i]) CUTRITON_RETURN_IF_ERROR(kernel->Compute(&ctx));
+  if (!state_->on_cuda()) {
+    // Host backends run synchronously; CPU timers record into the profiler.
+    s.profiler.Clear();
+    Profiler* profiler = plan.enable_profiling() ? &s.profiler : nullptr;
+    for (std::size_t i = 0; i < s.kernels.size(); ++i) {
+      const Node& node = graph.nodes().at(static_cast<std::size_t>(plan.ops()[i].node_id));
+      KernelContext context{&node, &s.tensors, stream, profiler, nullptr};
+      for (auto& kernel : s.kernels[i]) CUTRITON_RETURN_IF_ERROR(kernel->Compute(&context));
     }
-    run_pending_ = true;
+    s.pending = true;
     return Status::OK();
   }
 
-  auto* cuda = static_cast<CudaState*>(cuda_state_);
   const auto& api = drv::Get();
-  CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuCtxSetCurrent(cuda->context), "cuCtxSetCurrent"));
-  cuda->active_stream = stream == nullptr ? cuda->owned_stream : reinterpret_cast<CUstream>(stream);
-  const bool graphs = state_->plan.enable_cuda_graph();
-  const bool profiling = state_->plan.enable_profiling();
-  void* scratch = reinterpret_cast<void*>(cuda->error_device);
+  CUTRITON_RETURN_IF_ERROR(s.device->MakeCurrent());
+  s.stream = stream != nullptr ? static_cast<CUstream>(stream) : s.device->own_stream();
+  const bool use_graphs = plan.enable_cuda_graph();
+  const bool profiling = plan.enable_profiling() && s.device->has_events();
+  void* error_word = s.device->error_word_device();
 
-  auto enqueue = [&]() -> Status {
-    auto record = [&](CUevent e) {
-      return graphs ? drv::Check(api.cuEventRecordWithFlags(e, cuda->active_stream, CU_EVENT_RECORD_EXTERNAL),
-                                 "cuEventRecordWithFlags")
-                    : drv::Check(api.cuEventRecord(e, cuda->active_stream), "cuEventRecord");
+  const auto enqueue = [&]() -> Status {
+    const auto mark = [&](CUevent event) {
+      return use_graphs ? drv::Check(api.cuEventRecordWithFlags(event, s.stream, CU_EVENT_RECORD_EXTERNAL),
+                                     "cuEventRecordWithFlags")
+                        : drv::Check(api.cuEventRecord(event, s.stream), "cuEventRecord");
     };
-    for (std::size_t i = 0; i < kernels_.size(); ++i) {
-      const PlanOp& op = state_->plan.ops()[i];
-      const Node& node = ActiveGraph().nodes().at(static_cast<std::size_t>(op.node_id));
-      EventPair& events = cuda->events[i];
-      events.timed = profiling && node.op_type() != "Flatten";
-      if (events.timed) CUTRITON_RETURN_IF_ERROR(record(events.start));
-      KernelContext ctx{&node, &tensors_, cuda->active_stream, nullptr, scratch};
-      for (auto& kernel : kernels_[i]) CUTRITON_RETURN_IF_ERROR(kernel->Compute(&ctx));
-      if (events.timed) CUTRITON_RETURN_IF_ERROR(record(events.end));
+    for (std::size_t i = 0; i < s.kernels.size(); ++i) {
+      const Node& node = graph.nodes().at(static_cast<std::size_t>(plan.ops()[i].node_id));
+      const bool timed = profiling && s.timed[i];
+      if (timed) CUTRITON_RETURN_IF_ERROR(mark(s.device->op_start(i)));
+      KernelContext context{&node, &s.tensors, s.stream, nullptr, error_word};
+      for (auto& kernel : s.kernels[i]) CUTRITON_RETURN_IF_ERROR(kernel->Compute(&context));
+      if (timed) CUTRITON_RETURN_IF_ERROR(mark(s.device->op_end(i)));
     }
     return Status::OK();
   };
 
-  if (!graphs) {
+  if (!use_graphs) {
     CUTRITON_RETURN_IF_ERROR(enqueue());
-    run_pending_ = true;
+    s.pending = true;
     return Status::OK();
   }
 
-  std::ostringstream k;
-  k << "profile:" << selected_profile_ << "|workspace:" << (workspace_ ? workspace_->data() : nullptr);
-  for (const auto& name : ActiveGraph().inputs()) {
-    const Tensor& t = tensors_.at(name);
-    k << "|in:" << name << ':' << t.buffer()->data() << ':' << t.byte_offset();
-    for (int64_t d : t.desc().shape) k << ':' << d;
-  }
-  for (const auto& name : ActiveGraph().outputs()) {
-    const Tensor& t = tensors_.at(name);
-    k << "|out:" << name << ':' << t.buffer()->data() << ':' << t.byte_offset();
-  }
-  for (std::size_t i = 0; i < selected_candidates_.size(); ++i) {
-    k << "|candidate:" << state_->plan.ops()[i].candidates[selected_candidates_[i]].candidate_id;
-  }
-  const std::string key = k.str();
-  auto entry = std::find_if(cuda->graphs.begin(), cuda->graphs.end(),
-                            [&](const GraphEntry& g) { return g.key == key; });
-  if (entry == cuda->graphs.end()) {
-    GraphEntry fresh;
-    fresh.key = key;
-    CUTRITON_RETURN_IF_ERROR(drv::Check(
-        api.cuStreamBeginCapture(cuda->active_stream, CU_STREAM_CAPTURE_MODE_GLOBAL), "cuStreamBeginCapture"));
-    const Status captured = enqueue();
-    const Status ended = drv::Check(api.cuStreamEndCapture(cuda->active_stream, &fresh.graph), "cuStreamEndCapture");
-    if (!captured.ok() || !ended.ok()) {
-      if (fresh.graph != nullptr) api.cuGraphDestroy(fresh.graph);
-      return captured.ok() ? ended : captured;
-    }
-    const Status instantiated =
-        drv::Check(api.cuGraphInstantiateWithFlags(&fresh.exec, fresh.graph, 0), "cuGraphInstantiate");
-    if (!instantiated.ok()) {
-      api.cuGraphDestroy(fresh.graph);
-      return instantiated;
-    }
-    const std::size_t capacity = std::max<std::size_t>(1, state_->plan.cuda_graph_cache_capacity());
-    if (cuda->graphs.size() >= capacity) {
-      auto oldest = std::min_element(cuda->graphs.begin(), cuda->graphs.end(),
-                                     [](const GraphEntry& a, const GraphEntry& b) { return a.last_used < b.last_used; });
-      api.cuGraphExecDestroy(oldest->exec);
-      api.cuGraphDestroy(oldest->graph);
-      cuda->graphs.erase(oldest);
-    }
-    cuda->graphs.push_back(std::move(fresh));
-    entry = std::prev(cuda->graphs.end());
-  }
-  entry->last_used = ++cuda->clock;
-  CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuGraphLaunch(entry->exec, cuda->active_stream), "cuGraphLaunch"));
-  run_pending_ = true;
+  // Launch fingerprint: everything a captured graph has baked in.
+  std::vector<std::uint64_t> fingerprint;
+  const auto put = [&](std::uint64_t word) { fingerprint.push_back(word); };
+  const auto put_tensor = [&](const Tensor& t) {
+    put(reinterpret_cast<std::uintptr_t>(t.buffer()->data()));
+    put(t.byte_offset());
+    put(t.desc().shape.size());
+    for (int64_t d : t.desc().shape) put(static_cast<std::uint64_t>(d));
+  };
+  put(static_cast<std::uint64_t>(s.profile + 1));
+  put(reinterpret_cast<std::uintptr_t>(s.workspace == nullptr ? nullptr : s.workspace->data()));
+  for (const std::string& name : graph.inputs()) put_tensor(s.bound.at(name));
+  put(~0ull);
+  for (const std::string& name : graph.outputs()) put_tensor(s.bound.at(name));
+  put(~0ull);
+  for (std::size_t c : s.chosen) put(c);
+
+  CUgraphExec exec = nullptr;
+  CUTRITON_RETURN_IF_ERROR(s.graphs->Acquire(fingerprint, s.stream, enqueue, &exec));
+  CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuGraphLaunch(exec, s.stream), "cuGraphLaunch"));
+  s.pending = true;
   return Status::OK();
 }
 
 Status ExecutionContext::Synchronize() {
-  if (!run_pending_) return Status::OK();
-  if (state_->plan.backend_options().device.type != DeviceType::kCUDA) {
-    run_pending_ = false;
-    return Status::OK();
-  }
-  auto* cuda = static_cast<CudaState*>(cuda_state_);
+  Session& s = *session_;
+  if (!s.pending) return Status::OK();
+  s.pending = false;
+  if (!state_->on_cuda()) return Status::OK();
   const auto& api = drv::Get();
-  run_pending_ = false;
-  CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuCtxSetCurrent(cuda->context), "cuCtxSetCurrent"));
-  CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuStreamSynchronize(cuda->active_stream), "cuStreamSynchronize"));
-  if (cuda->error_host->code != 0) {
-    std::ostringstream message;
-    message << "a kernel abandoned a bounded wait (code " << cuda->error_host->code << ", site "
-            << cuda->error_host->site << ", block " << cuda->error_host->block << ")";
-    std::memset(cuda->error_host, 0, sizeof(ErrorBlock));
-    return Status::RuntimeError(message.str());
-  }
-  profiler_.Clear();
-  if (state_->plan.enable_profiling()) {
-    for (std::size_t i = 0; i < state_->plan.ops().size(); ++i) {
-      const PlanOp& op = state_->plan.ops()[i];
-      const EventPair& events = cuda->events[i];
-      float ms = 0.0f;
-      if (events.timed) {
-        CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuEventElapsedTime(&ms, events.start, events.end), "cuEventElapsedTime"));
-      }
-      profiler_.Record(op.node_name, op.backend_name, static_cast<double>(ms));
+  CUTRITON_RETURN_IF_ERROR(s.device->MakeCurrent());
+  CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuStreamSynchronize(s.stream), "cuStreamSynchronize"));
+  CUTRITON_RETURN_IF_ERROR(s.device->TakeDeviceError());
+  s.profiler.Clear();
+  if (!state_->plan.enable_profiling()) return Status::OK();
+  const auto& ops = state_->plan.ops();
+  for (std::size_t i = 0; i < ops.size(); ++i) {
+    float ms = 0.0f;
+    if (s.device->has_events() && i < s.timed.size() && s.timed[i]) {
+      CUTRITON_RETURN_IF_ERROR(
+          drv::Check(api.cuEventElapsedTime(&ms, s.device->op_start(i), s.device->op_end(i)), "cuEventElapsedTime"));
     }
+    s.profiler.Record(ops[i].node_name, ops[i].backend_name, static_cast<double>(ms));
   }
   return Status::OK();
-}
-
-void ExecutionContext::InvalidateCudaGraph() {
-  auto* cuda = static_cast<CudaState*>(cuda_state_);
-  if (cuda == nullptr) return;
-  drv::Get().cuCtxSetCurrent(cuda->context);
-  DestroyGraphs(cuda);
 }
 
 }  // namespace cutriton

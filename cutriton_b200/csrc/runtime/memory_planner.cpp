@@ -1,10 +1,23 @@
-// Single-workspace memory planner.
+// Workspace planner for the intermediate tensors of one graph.
 //
-// Same policy as the reference planner (src/runtime/memory_planner.cpp:29-169):
-// graph inputs/outputs and constants are external; every other value gets a
-// 256-byte aligned slot; a slot is freed once the value's last consumer ran
-// and reused best-fit (smallest free block that fits, split when larger);
-// Flatten outputs alias their input and extend its lifetime.
+// Contract (include/cutriton/runtime/memory_planner.h): graph inputs, graph
+// outputs and constants live outside the workspace; every other value gets a
+// 256-byte aligned range that no value alive at the same time overlaps; a
+// Flatten output is a view of its input (same range, and the input stays
+// alive as long as the view is read).
+//
+// Method: an offline interval plan rather than a free list walked in node
+// order.
+//   1. Lifetimes. A value is alive from the node that writes it to the last
+//      node that reads it, inclusive (a node's inputs and outputs never
+//      share memory); a Flatten view extends its source's lifetime.
+//   2. Placement, largest value first (ties: earlier definition first): each
+//      value takes the lowest aligned offset that overlaps no placed value
+//      whose lifetime intersects its own. Sorting by size keeps big tensors
+//      packed at the bottom and lets small short-lived ones fill the gaps.
+//   3. Views take their source's range. Allocations are reported in
+//      definition order; `reused` marks a range that an earlier value with a
+//      disjoint lifetime also occupied.
 
 #include "cutriton/runtime/memory_planner.h"
 
@@ -15,122 +28,163 @@
 namespace cutriton {
 namespace {
 
-constexpr std::size_t kAlignment = 256;
+constexpr std::size_t kAlign = 256;
 
-std::size_t AlignUp(std::size_t bytes) { return (bytes + kAlignment - 1) / kAlignment * kAlignment; }
+std::size_t RoundUp(std::size_t bytes) { return (bytes + kAlign - 1) / kAlign * kAlign; }
 
-struct Block {
-  std::size_t offset;
-  std::size_t size;
+struct Interval {
+  std::string name;
+  int first{0};           // node that writes the value
+  int last{0};            // last node that reads it (>= first)
+  std::size_t bytes{0};   // tensor bytes
+  std::size_t span{0};    // bytes rounded up to the alignment
+  std::size_t offset{0};
+  std::string view_of;    // non-empty for a Flatten view
+  std::size_t order{0};   // definition order
 };
+
+bool Overlap(std::size_t a, std::size_t a_len, std::size_t b, std::size_t b_len) {
+  return a < b + b_len && b < a + a_len;
+}
 
 }  // namespace
 
 Status MemoryPlanner::Plan(const Graph& graph, MemoryPlan* plan) const {
-  if (plan == nullptr) return Status::InvalidArgument("MemoryPlan output pointer is null");
+  if (plan == nullptr) return Status::InvalidArgument("MemoryPlanner::Plan: no MemoryPlan to write");
   *plan = MemoryPlan{};
-  std::unordered_set<std::string> external(graph.inputs().begin(), graph.inputs().end());
-  external.insert(graph.outputs().begin(), graph.outputs().end());
+  const auto& nodes = graph.nodes();
+  const int end_of_graph = static_cast<int>(nodes.size());
 
-  std::unordered_map<std::string, std::string> alias_source;
-  for (const auto& node : graph.nodes()) {
-    if (node.op_type() == "Flatten" && node.inputs().size() == 1 && node.outputs().size() == 1) {
-      alias_source[node.outputs()[0]] = node.inputs()[0];
-    }
-  }
+  std::unordered_set<std::string> outside(graph.inputs().begin(), graph.inputs().end());
+  for (const auto& name : graph.outputs()) outside.insert(name);
 
-  // Index of the last node that reads each value (outputs: past the end).
+  // ---- 1. lifetimes ---------------------------------------------------------
+  std::vector<Interval> values;
+  std::unordered_map<std::string, std::size_t> index;  // name -> position in `values`
   std::unordered_map<std::string, int> last_read;
-  const int node_count = static_cast<int>(graph.nodes().size());
-  for (int i = 0; i < node_count; ++i) {
-    const Node& node = graph.nodes()[static_cast<std::size_t>(i)];
-    for (const auto& v : node.inputs()) last_read[v] = i;
-    for (const auto& v : node.outputs()) last_read.emplace(v, i);
+  for (int at = 0; at < end_of_graph; ++at) {
+    for (const auto& name : nodes[at].inputs()) last_read[name] = at;
   }
-  for (const auto& v : graph.outputs()) last_read[v] = node_count;
-  for (const auto& entry : alias_source) {
-    const auto alias = last_read.find(entry.first);
-    if (alias != last_read.end()) {
-      int& source = last_read[entry.second];
-      source = std::max(source, alias->second);
-    }
-  }
+  for (const auto& name : graph.outputs()) last_read[name] = end_of_graph;
 
-  std::vector<Block> free_list;
-  std::vector<std::pair<std::string, Block>> live;
-  std::unordered_map<std::string, Allocation> placed;
-  std::size_t high_water = 0;
-
-  for (int i = 0; i < node_count; ++i) {
-    // Retire values whose last reader ran before this node.
-    for (auto it = live.begin(); it != live.end();) {
-      const auto use = last_read.find(it->first);
-      if (use != last_read.end() && use->second < i) {
-        free_list.push_back(it->second);
-        it = live.erase(it);
-      } else {
-        ++it;
-      }
-    }
-    const Node& node = graph.nodes()[static_cast<std::size_t>(i)];
+  for (int at = 0; at < end_of_graph; ++at) {
+    const Node& node = nodes[at];
+    const bool is_view = node.op_type() == "Flatten" && node.inputs().size() == 1 && node.outputs().size() == 1;
     for (const auto& name : node.outputs()) {
-      if (external.count(name) != 0) continue;
-      const auto alias = alias_source.find(name);
-      if (alias != alias_source.end()) {
-        const auto source = placed.find(alias->second);
-        Allocation a;
-        if (source != placed.end()) {
-          a = source->second;
-        } else {
-          if (external.count(alias->second) == 0) {
-            return Status::Internal("Flatten alias source has no allocation: " + alias->second);
-          }
-          const ValueDesc* src = graph.FindValue(alias->second);
-          if (src == nullptr) return Status::Internal("Flatten alias source is unknown: " + alias->second);
-          a.size_bytes = src->tensor.ByteSize();
-        }
-        a.value_name = name;
-        a.alias_of = alias->second;
-        a.reused = true;
-        const ValueDesc* value = graph.FindValue(name);
-        if (value == nullptr || value->tensor.ByteSize() != a.size_bytes) {
-          return Status::ShapeError("Flatten alias changes the tensor byte size: " + name);
-        }
-        plan->allocations.push_back(a);
-        placed.emplace(name, a);
-        continue;
+      if (outside.count(name) != 0 || index.count(name) != 0) continue;
+      const ValueDesc* desc = graph.FindValue(name);
+      if (desc == nullptr || (desc->is_constant && !is_view)) continue;
+      Interval v;
+      v.name = name;
+      v.first = at;
+      const auto read = last_read.find(name);
+      v.last = read == last_read.end() ? at : std::max(at, read->second);
+      v.bytes = desc->tensor.ByteSize();
+      v.order = values.size();
+      if (is_view) {
+        v.view_of = node.inputs()[0];
+      } else if (v.bytes == 0) {
+        return Status::ShapeError("MemoryPlanner::Plan: '" + name + "' has no static size (unresolved shape)");
       }
-      const ValueDesc* value = graph.FindValue(name);
-      if (value == nullptr || value->is_constant) continue;
-      const std::size_t bytes = value->tensor.ByteSize();
-      if (bytes == 0) return Status::ShapeError("cannot plan memory for a dynamically sized value: " + name);
-      const std::size_t reserved = AlignUp(bytes);
-      auto best = free_list.end();
-      for (auto it = free_list.begin(); it != free_list.end(); ++it) {
-        if (it->size >= reserved && (best == free_list.end() || it->size < best->size)) best = it;
-      }
-      Allocation a;
-      a.value_name = name;
-      a.size_bytes = bytes;
-      if (best != free_list.end()) {
-        a.offset = best->offset;
-        a.reused = true;
-        if (best->size > reserved) {
-          best->offset += reserved;
-          best->size -= reserved;
-        } else {
-          free_list.erase(best);
-        }
-      } else {
-        a.offset = AlignUp(high_water);
-        high_water = a.offset + reserved;
-      }
-      plan->allocations.push_back(a);
-      placed.emplace(name, a);
-      live.push_back({name, Block{a.offset, reserved}});
+      v.span = RoundUp(v.bytes);
+      index.emplace(name, values.size());
+      values.push_back(std::move(v));
     }
   }
-  plan->workspace_size_bytes = AlignUp(high_water);
+  // Views keep their source alive. A view is defined after its source, so
+  // walking back to front carries the lifetime of a chain of views down to
+  // the planned value at its root.
+  for (auto v = values.rbegin(); v != values.rend(); ++v) {
+    if (v->view_of.empty()) continue;
+    const auto source = index.find(v->view_of);
+    if (source != index.end()) {
+      Interval& s = values[source->second];
+      s.last = std::max(s.last, v->last);
+    }
+  }
+  for (Interval& v : values) {
+    if (v.view_of.empty()) continue;
+    const auto source = index.find(v.view_of);
+    if (source != index.end()) {
+      const Interval& s = values[source->second];
+      if (s.bytes != v.bytes) {
+        return Status::ShapeError("MemoryPlanner::Plan: Flatten view '" + v.name + "' has " +
+                                  std::to_string(v.bytes) + " bytes, its source " + std::to_string(s.bytes));
+      }
+      continue;
+    }
+    // A view of a graph input lives outside the workspace like its source.
+    if (outside.count(v.view_of) == 0) {
+      return Status::Internal("MemoryPlanner::Plan: the source of Flatten view '" + v.name +
+                              "' is neither planned nor external: " + v.view_of);
+    }
+    const ValueDesc* src = graph.FindValue(v.view_of);
+    if (src == nullptr || src->tensor.ByteSize() != v.bytes) {
+      return Status::ShapeError("MemoryPlanner::Plan: Flatten view '" + v.name + "' changes the byte size");
+    }
+  }
+
+  // ---- 2. placement, largest first --------------------------------------------
+  std::vector<std::size_t> by_size;
+  for (std::size_t i = 0; i < values.size(); ++i) {
+    if (values[i].view_of.empty()) by_size.push_back(i);
+  }
+  std::stable_sort(by_size.begin(), by_size.end(),
+                   [&](std::size_t a, std::size_t b) { return values[a].span > values[b].span; });
+  std::vector<std::size_t> placed;
+  std::size_t top = 0;
+  for (std::size_t i : by_size) {
+    Interval& v = values[i];
+    // Ranges taken by placed values alive at the same time, sorted by offset.
+    std::vector<std::pair<std::size_t, std::size_t>> busy;
+    for (std::size_t j : placed) {
+      const Interval& u = values[j];
+      if (u.first <= v.last && v.first <= u.last) busy.emplace_back(u.offset, u.span);
+    }
+    std::sort(busy.begin(), busy.end());
+    std::size_t candidate = 0;
+    for (const auto& range : busy) {
+      if (Overlap(candidate, v.span, range.first, range.second)) {
+        candidate = std::max(candidate, RoundUp(range.first + range.second));
+      }
+    }
+    v.offset = candidate;
+    top = std::max(top, candidate + v.span);
+    placed.push_back(i);
+  }
+
+  // ---- 3. report -----------------------------------------------------------------
+  for (const Interval& v : values) {
+    Allocation a;
+    a.value_name = v.name;
+    a.size_bytes = v.bytes;
+    if (!v.view_of.empty()) {
+      // Offset of the planned value at the root of the chain of views (0
+      // for a view of an external value, which the engine binds directly).
+      std::size_t offset = 0;
+      for (auto at = index.find(v.view_of); at != index.end(); at = index.find(values[at->second].view_of)) {
+        offset = values[at->second].offset;
+        if (values[at->second].view_of.empty()) break;
+      }
+      a.offset = offset;
+      a.alias_of = v.view_of;
+      a.reused = true;
+      plan->allocations.push_back(std::move(a));
+      continue;
+    }
+    a.offset = v.offset;
+    // Reused: an earlier-defined value with a disjoint lifetime sat here.
+    for (const Interval& u : values) {
+      if (u.order >= v.order) break;
+      if (!u.view_of.empty()) continue;
+      if (Overlap(u.offset, u.span, v.offset, v.span) && !(u.first <= v.last && v.first <= u.last)) {
+        a.reused = true;
+        break;
+      }
+    }
+    plan->allocations.push_back(std::move(a));
+  }
+  plan->workspace_size_bytes = RoundUp(top);
   return Status::OK();
 }
 

@@ -297,7 +297,19 @@ def _pool_specs() -> list[KernelSpec]:
             kernel_id="global_average_pool.fp32.nchw", op_type="GlobalAveragePool", version=1, source="pool.cu",
             symbol="ctb_global_average_pool_f32", arguments=gap_arguments, layout="NCHW",
             grid=(ceil_div(out_numel(), meta("PLANES")),),
-            variants=(Variant("warp_per_plane", num_warps=8, meta={"PLANES": 8}, default=True),),
+            variants=(Variant("warp_per_plane", num_warps=8, meta={"PLANES": 8}, default=False),),
+        ),
+        # Planes of at most 81 elements (9x9): 128 planes per block staged in
+        # shared memory by cp.async, one serial sum per thread.
+        KernelSpec(
+            kernel_id="global_average_pool_staged.fp32.nchw", op_type="GlobalAveragePool", version=1,
+            source="pool.cu", symbol="ctb_global_average_pool_f32_staged", arguments=gap_arguments, layout="NCHW",
+            grid=(ceil_div(out_numel(), meta("PLANES")),),
+            constraints=(
+                {"kind": "dim_le", "source": "input", "index": 0, "axis": 2, "value": 9},
+                {"kind": "dim_le", "source": "input", "index": 0, "axis": 3, "value": 9},
+            ),
+            variants=(Variant("block_of_128_planes", num_warps=4, meta={"PLANES": 128}, default=True),),
         ),
     ]
 

@@ -57,43 +57,35 @@ class ExecutionContext {
   // Waits for the pending run, collects profiling events and checks the
   // device-side error word of the kernels (bounded waits that expired).
   Status Synchronize();
-  bool run_pending() const { return run_pending_; }
+  bool run_pending() const;
 
-  const Profiler& profiler() const { return profiler_; }
+  const Profiler& profiler() const;
   std::size_t cached_cuda_graph_count() const;
   std::size_t loaded_cuda_module_count() const;
-  const std::unordered_map<std::string, Tensor>& tensors() const { return tensors_; }
+  // Every tensor the plan touches: bound inputs/outputs, device constants and
+  // the workspace views of the intermediates (valid after the first run).
+  const std::unordered_map<std::string, Tensor>& tensors() const;
   // Candidate index chosen for each plan op (after the first run).
-  const std::vector<std::size_t>& selected_candidates() const { return selected_candidates_; }
+  const std::vector<std::size_t>& selected_candidates() const;
   // Pins plan op `op` to candidate `candidate`, overriding the default and
   // the tuner for this context (used to test every variant; extension).
   Status SelectCandidate(std::size_t op, std::size_t candidate);
 
  private:
-  Status PrepareKernels();
-  Status PrepareTuning();
+  // Lazy preparation stages of RunAsync; each rebuilds only what changed.
   Status PrepareTensors();
   Status ValidateBindings() const;
+  Status PrepareTuning();
+  Status PrepareKernels();
   void InvalidateCudaGraph();
   const Graph& ActiveGraph() const;
   const MemoryPlan& ActiveMemoryPlan() const;
 
+  // All mutable per-context state (shapes, bindings, workspace, kernels,
+  // device resources); defined in the runtime, so this header needs no CUDA.
+  struct Session;
   std::shared_ptr<EngineState> state_;
-  bool kernels_prepared_{false};
-  bool tensors_prepared_{false};
-  bool run_pending_{false};
-  bool tuning_prepared_{false};
-  std::vector<std::size_t> selected_candidates_;
-  std::unordered_map<std::size_t, std::size_t> pinned_candidates_;
-  int selected_profile_{-1};
-  std::unordered_map<std::string, std::vector<int64_t>> input_shapes_;
-  Graph resolved_graph_;
-  bool shapes_resolved_{false};
-  std::vector<std::vector<std::unique_ptr<OpKernel>>> kernels_;
-  std::unordered_map<std::string, Tensor> tensors_;
-  std::shared_ptr<Buffer> workspace_;
-  Profiler profiler_;
-  void* cuda_state_{nullptr};
+  std::unique_ptr<Session> session_;
 };
 
 }  // namespace cutriton

@@ -140,15 +140,26 @@ def test_max_pool_nan_bitexact(cuda, shape):
         assert_bitexact(out["y"], expected, f"MaxPool NaN {cand}")
 
 
-@pytest.mark.parametrize("shape", [(4, 2048, 7, 7), (3, 17, 5, 3)])
+@pytest.mark.parametrize("shape", [(4, 2048, 7, 7), (3, 17, 5, 3), (3, 50, 9, 9), (2, 3, 10, 10)])
 def test_global_average_pool(cuda, shape):
+    """Every candidate; the staged kernel sums each plane serially like the
+    reference (resnet.py:185-198) and the oracle, so it must match bit for
+    bit; the warp-per-plane kernel sums in a tree (1e-5 relative)."""
     x = randn(*shape)
     model = ct.Model()
     model.add_input("x", list(shape))
     model.add_node("gap", "GlobalAveragePool", ["x"], ["y"])
     model.add_output("y")
-    out, _ = run_graph(model, {"x": x}, {"y": ((shape[0], shape[1], 1, 1), np.float32)})
-    assert_close(out["y"], oracle.global_average_pool(x), atol=1e-6, rtol=1e-5, what="GAP")
+    expected = oracle.global_average_pool(x)
+    engine = ct.build_engine(model)
+    candidates = engine.ops()[0]["candidates"]
+    assert any("staged" in c for c in candidates) == (shape[2] <= 9 and shape[3] <= 9)
+    for index, cand in enumerate(candidates):
+        out, _ = run_graph(model, {"x": x}, {"y": ((shape[0], shape[1], 1, 1), np.float32)}, candidate=(0, index))
+        if "staged" in cand:
+            assert_bitexact(out["y"], expected, f"GAP {cand}")
+        else:
+            assert_close(out["y"], expected, atol=1e-6, rtol=1e-5, what=f"GAP {cand}")
 
 
 @pytest.mark.parametrize("numel_shape", [(2, 64, 56, 56), (1, 3, 7, 5), (4099,)])
