@@ -318,6 +318,11 @@ def run_config2(args, tuning: str = "TuneOnMiss") -> dict:
     ops = engine.ops()
     chosen = [op["candidates"][ctx.selected_candidate(i)] for i, op in enumerate(ops)]
     unfused = sum(1 for c in chosen if c.startswith(UNFUSED))
+    # Which ops the tuner moved off their default candidate at the last batch
+    # run (128; each batch shape is tuned on its first run and cached).
+    moved = [{"op": op["node"], "default": op["candidates"][op["default"]].split(":", 1)[-1],
+              "chosen": chosen[i].split(":", 1)[-1]}
+             for i, op in enumerate(ops) if ctx.selected_candidate(i) != op["default"]]
     kinds: dict[str, int] = {}
     for c in chosen:
         kind = c.split(":")[1] if ":" in c else c
@@ -326,7 +331,7 @@ def run_config2(args, tuning: str = "TuneOnMiss") -> dict:
             "higher_is_better": True, "config": {"workload": "resnet50_dynamic_batch", "profile": [1, 32, 128],
                                                 "graph_lru": 4, "tuning": tuning},
             "batches": results, "cached_graphs": ctx.cached_graph_count(), "ops": engine.num_ops(),
-            "ops_tuned_to_unfused": unfused, "selected_kernels": kinds}
+            "ops_tuned_to_unfused": unfused, "selected_kernels": kinds, "tuned_off_default": moved}
 
 
 def run_config3(args, peaks) -> dict:

@@ -272,6 +272,8 @@ Status ExecutionContext::BindInput(const std::string& name, Tensor tensor) {
   const bool needs_resolve = !state_->plan.profile_plans().empty() && !session_->resolved_ok;
   CUTRITON_RETURN_IF_ERROR(
       CheckBoundary(session_->pending, needs_resolve, ActiveGraph(), ActiveGraph().inputs(), "input", name, tensor));
+  // Visible through tensors() at once, before the next run rebuilds the table.
+  session_->tensors[name] = tensor;
   session_->bound[name] = std::move(tensor);
   ++session_->binding;
   return Status::OK();
@@ -282,6 +284,7 @@ Status ExecutionContext::BindOutput(const std::string& name, Tensor tensor) {
   const bool needs_resolve = !state_->plan.profile_plans().empty() && !session_->resolved_ok;
   CUTRITON_RETURN_IF_ERROR(
       CheckBoundary(session_->pending, needs_resolve, ActiveGraph(), ActiveGraph().outputs(), "output", name, tensor));
+  session_->tensors[name] = tensor;
   session_->bound[name] = std::move(tensor);
   ++session_->binding;
   return Status::OK();
