@@ -193,7 +193,9 @@ def _conv_specs() -> list[KernelSpec]:
                 defines={**tm_defines(2, 4, 4, 2, 0), "CTB_TM_WINDOW": "1"},
                 meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128},
                 constraints=({"kind": "dim_le", "source": "input", "index": 1, "axis": 1, "value": 4},),
-                arg_overrides={k: v for k, v in {**overrides, **boxes(0, 64, 0)}.items() if k in arg_names}))
+                # Its own window map keeps the full box (the tiny box is for the
+                # variants that never load a window).
+                arg_overrides={k: v for k, v in boxes(0, 64, 0).items() if k in arg_names}))
         specs.append(KernelSpec(
             kernel_id=kernel_id.replace("tcgen05", "tcgen05_tmem"), op_type=op_type, version=1,
             source="conv_tm.cu", symbol=symbol.replace("_tc", "_tm"),

@@ -194,3 +194,20 @@ def test_launch_shapes_match_the_kernels():
                 assert need <= variant.shared_memory_bytes <= 232448, (spec.kernel_id, variant.variant_id)
                 checked.add(spec.source)
     assert checked == {"gemm_f16_tp.cu", "conv_tm.cu"}
+
+
+def test_window_variant_keeps_its_full_window_box():
+    """The stem's input-window variant loads {232 columns, 11 rows, 4
+    channels, 1 image} per tile and waits for exactly that many bytes; the
+    other variants of its family bind the window map with a tiny unused box.
+    A variant that loads windows must never get the tiny box."""
+    import json
+
+    from cutriton_b200 import _build
+
+    pack = json.loads((_build.PACK_DIR / "pack.json").read_text())  # built by the session fixture
+    window = [k for k in pack["kernels"] if k["variant_id"].endswith("_window")]
+    assert window
+    for entry in window:
+        boxes = [a["source"]["box"] for a in entry["arguments"] if a["name"] == "tma_xwin"]
+        assert boxes == [[232, 11, 4, 1]], (entry["kernel_id"], boxes)
