@@ -43,10 +43,8 @@
 //   warps 2-5 — epilogue of the previous tile while the next one computes:
 //       lane = pixel, 32 channels per TMEM load; BN affine
 //       (x - mean) * rsqrt(var + eps) * scale + bias (python/cutriton/
-//       triton_kernels/resnet.py:41-47), optional residual add and ReLU; each
-//       warp moves its own 32 pixels x 32 channels per chunk by tensor
-//       copies through a private staging ring, with no barrier between the
-//       warps inside a tile.
+//       triton_kernels/resnet.py:41-47), optional residual add and ReLU, stores
+//       of 32 consecutive pixels per channel.
 // All waits are bounded (see tc_common.cuh).
 
 #include "tc_common.cuh"
@@ -71,23 +69,6 @@ constexpr int kGatherGroups = CTB_TM_GATHER_GROUPS;
 #define CTB_TM_EPI_WARPS 4
 #endif
 constexpr int kEpiWarps = CTB_TM_EPI_WARPS;
-// Epilogue data movement (tensor-copy path): 0 — the four warps fill one
-// [32 channels][128 pixels] slot per chunk together (named barriers) and one
-// thread stores it; 1 — each warp stores its own pixels through a private
-// ring, in boxes of CTB_TM_EPI_BOX_C channels (32 or 64).
-#ifndef CTB_TM_EPI_MODE
-#define CTB_TM_EPI_MODE 1
-#endif
-#ifndef CTB_TM_EPI_BOX_C
-#define CTB_TM_EPI_BOX_C 64
-#endif
-// Activation boxes of the 1x1 variant: 0 — one {128 pixels, 32 channels} box
-// per k block for tiles in one image (global loads otherwise); 1 — one
-// {32 pixels, 32 channels} box per TMEM lane quarter whose pixels lie in one
-// image (global loads for the others).
-#ifndef CTB_TM_A_QUARTER
-#define CTB_TM_A_QUARTER 0
-#endif
 constexpr int kHalves = kEpiWarps / 4;
 static_assert(kEpiWarps == 4 || kEpiWarps == 8, "epilogue warps");
 
@@ -212,7 +193,7 @@ struct __align__(8) Barriers {
   uint64_t empty_b[kMaxStages];  // shared-memory weight stage consumed by the MMAs
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
-  uint64_t residual_full[24];  // residual loads: per epilogue warp, one per staging slot
+  uint64_t residual_full[6];  // bulk residual loads, one per staging slot
   uint64_t a_full[kARing];    // activation ring (1x1 variant): TMA landed / no-copy arrival
   uint64_t a_empty[kARing];   // activation ring: the gather group has read the block
   uint64_t win_full[2];       // input windows (small-channel variant)
@@ -222,7 +203,7 @@ struct __align__(8) Barriers {
   int abort;
   int consumed;
 };
-constexpr uint32_t kBarrierBytes = 640;
+constexpr uint32_t kBarrierBytes = 512;
 static_assert(sizeof(Barriers) <= kBarrierBytes, "barrier block");
 
 // 32 lanes x 32 consecutive 32-bit columns from registers: thread t of the
@@ -402,33 +383,19 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
   };
   const long long tiles = m_tiles * co_tiles;
   const int my_tiles = tiles > blockIdx.x ? static_cast<int>((tiles - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
-  // 1x1 variant: in a 1x1 / stride-1 / unpadded convolution, each TMEM lane
-  // quarter (32 pixels) of a tile whose pixels are all valid and in one image
-  // takes its activation blocks by TMA: box {32 pixels, 32 channels} of the
-  // [N][C][H*W] view (tma_x is encoded exactly when the planes are 16-byte
-  // aligned, which a_tma_shape checks too). Per quarter rather than per tile,
-  // so layers whose tiles straddle images (14x14: two of three tiles) still
-  // take most blocks by TMA.
+  // 1x1 variant: tiles of a 1x1 / stride-1 / unpadded convolution that lie in
+  // one image take their activation blocks by TMA (tma_x is encoded exactly
+  // when the planes are 16-byte aligned, which a_tma_shape checks too).
   const bool a_tma_shape = CTB_TM_A_TMA && p.r == 1 && p.s == 1 && p.stride_h == 1 && p.stride_w == 1 &&
                            p.pad_h == 0 && p.pad_w == 0 && p.c % kBK == 0 && (p.h * p.w) % 4 == 0 &&
                            (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-  auto quarter_a_tma = [&](long long tile, int quarter, int* hw0, int* img) {
+  auto tile_a_tma = [&](long long tile, int* hw0, int* img) {
     if (!a_tma_shape) return false;
-    const long long mt = tile / co_tiles;
-    if (!CTB_TM_A_QUARTER) {
-      // One {128 pixels} box serves every quarter when the tile lies in one image.
-      const long long t0 = tile_p0(mt);
-      const long long im = t0 / pixels_per_image;
-      *hw0 = static_cast<int>(t0 - im * pixels_per_image);
-      *img = static_cast<int>(im);
-      return *hw0 + tile_rows(mt) <= pixels_per_image;
-    }
-    if (quarter * 32 + 32 > tile_rows(mt)) return false;
-    const long long p0 = tile_p0(mt) + quarter * 32;
+    const long long p0 = tile_p0(tile / co_tiles);
     const long long im = p0 / pixels_per_image;
     *hw0 = static_cast<int>(p0 - im * pixels_per_image);
     *img = static_cast<int>(im);
-    return *hw0 + 32 <= pixels_per_image;
+    return *hw0 + tile_rows(tile / co_tiles) <= pixels_per_image;
   };
   // Bulk / tensor-copy epilogue: needs 16-byte aligned rows of every channel
   // plane, the same condition under which the host encodes tma_out / tma_res
@@ -449,11 +416,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       mbar_init(&bars->tmem_full[b], 1);
       mbar_init(&bars->tmem_empty[b], kEpiWarps);
     }
-    if (CTB_TM_EPI_MODE == 0) {
-      for (int b = 0; b < kSlots; ++b) mbar_init(&bars->residual_full[b], 32);  // 8 issuing lanes x 4 warps of a half
-    } else {
-      for (int b = 0; b < 4 * kSlots; ++b) mbar_init(&bars->residual_full[b], 1);  // lane 0 of the owning warp
-    }
+    for (int b = 0; b < kSlots; ++b) mbar_init(&bars->residual_full[b], 32);  // 8 issuing lanes x 4 warps of a half
     for (int b = 0; b < kARing; ++b) {
       mbar_init(&bars->a_full[b], 1);
       mbar_init(&bars->a_empty[b], kGroupThreads);
@@ -532,7 +495,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       const int kb = item - local * k_blocks;
       const long long tile = blockIdx.x + static_cast<long long>(local) * gridDim.x;
       int hw0, img;
-      if (quarter_a_tma(tile, warp & 3, &hw0, &img)) return true;  // arrives by TMA; read in publish
+      if (tile_a_tma(tile, &hw0, &img)) return true;  // arrives by TMA; read in publish
       if (window_shape) {
         // Every tile passes its buffer through the window barriers (a
         // no-copy arrival when it uses the global-load gather), so each
@@ -601,18 +564,10 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
         const int sa = item % kARing;
         if (!mbar_wait(&bars->a_full[sa], (item / kARing) & 1, abort, scratch, 40)) return false;
         int hw0, img;
-        if (quarter_a_tma(blockIdx.x + static_cast<long long>(item / k_blocks) * gridDim.x, warp & 3, &hw0, &img)) {
-          if (CTB_TM_A_QUARTER) {
-            // The quarter's box: [32 channels][32 pixels].
-            const float* blk = a_ring + sa * kBK * kBM + (warp & 3) * (kBK * 32) + lane;
+        if (tile_a_tma(blockIdx.x + static_cast<long long>(item / k_blocks) * gridDim.x, &hw0, &img)) {
+          const float* blk = a_ring + sa * kBK * kBM + row;
 #pragma unroll
-            for (int kk = 0; kk < kBK; ++kk) v[kk] = blk[kk * 32];
-          } else {
-            // The tile's box: [32 channels][128 pixels].
-            const float* blk = a_ring + sa * kBK * kBM + row;
-#pragma unroll
-            for (int kk = 0; kk < kBK; ++kk) v[kk] = blk[kk * kBM];
-          }
+          for (int kk = 0; kk < kBK; ++kk) v[kk] = blk[kk * kBM];
         }
         mbar_arrive(&bars->a_empty[sa]);
       }
@@ -678,11 +633,8 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
     for (int local = 0; local < my_tiles && !stop; ++local) {
       const long long tile = blockIdx.x + static_cast<long long>(local) * gridDim.x;
       const int co0 = static_cast<int>(tile % co_tiles) * BN;
-      // Quarters of this tile whose activation blocks come by TMA.
-      int a_hw0[4] = {0, 0, 0, 0}, a_img[4] = {0, 0, 0, 0};
-      uint32_t a_quarters = 0;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) a_quarters |= quarter_a_tma(tile, q, &a_hw0[q], &a_img[q]) ? 1u << q : 0u;
+      int a_hw0 = 0, a_img = 0;
+      const bool tile_uses_a_tma = tile_a_tma(tile, &a_hw0, &a_img);
       if (window_shape && local == 0 && !issue_window(0)) break;
       for (int kb = 0; kb < k_blocks; ++kb, ++g) {
         const int s = g % kStages;
@@ -704,18 +656,9 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
             ++g;
             break;
           }
-          if (!CTB_TM_A_QUARTER && a_quarters == 0xFu) {
+          if (tile_uses_a_tma) {
             mbar_arrive_expect_tx(&bars->a_full[sa], kBK * kBM * 4);
-            tma_load_3d(a_ring + sa * kBK * kBM, tma_x, &bars->a_full[sa], a_hw0[0], kb * kBK, a_img[0]);
-          } else if (CTB_TM_A_QUARTER && a_quarters != 0) {
-            mbar_arrive_expect_tx(&bars->a_full[sa], __popc(a_quarters) * kBK * 32 * 4);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              if (a_quarters & (1u << q)) {
-                tma_load_3d(a_ring + sa * kBK * kBM + q * (kBK * 32), tma_x, &bars->a_full[sa], a_hw0[q], kb * kBK,
-                            a_img[q]);
-              }
-            }
+            tma_load_3d(a_ring + sa * kBK * kBM, tma_x, &bars->a_full[sa], a_hw0, kb * kBK, a_img);
           } else {
             mbar_arrive(&bars->a_full[sa]);
           }
@@ -854,7 +797,7 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
       }
     };
 
-    if (bulk_epilogue && CTB_TM_EPI_MODE == 0) {
+    if (bulk_epilogue) {
       // Bulk path: every 4-pixel group lies inside one image, so each channel
       // row of a tile is one or a few 16-byte-aligned runs in global memory.
       // Chunks (32 channels of a tile) go through a ring of kSlots staging
@@ -999,158 +942,6 @@ __device__ __forceinline__ void conv_tm(uint8_t* smem, const TmaDescriptor* tma_
           if (h % kHalves != half) continue;
           volatile int never = 0;
           mbar_wait(&bars->residual_full[h % kSlots], (h / kSlots) & 1, &never, scratch, 39);
-        }
-      }
-    } else if (bulk_epilogue) {
-      // Per-warp pipelines. Warp `quarter` owns TMEM lanes (= tile pixels)
-      // 32q..32q+31 and walks the tiles on its own, with no barrier between
-      // the epilogue warps inside a tile. Its output leaves in boxes of
-      // {32 pixels, kBoxC channels, 1 image} of the [N][K][H*W] view; box
-      // unit u (u = local tile * boxes per tile + b) goes through buffer
-      // u % kBufs of the warp's private staging ([kBoxC channels][32 pixels]
-      // FP32). When the warp's 32 pixels lie in one image the residual box is
-      // loaded kAheadU units early into the buffer, the results are written
-      // back in place and leave with one store; a warp range that straddles
-      // two images (or runs past the last pixel) uses plain loads and stores
-      // for that unit. Every unit commits one bulk group and arrives once on
-      // its buffer's barrier (with or without a copy), so buffer phases and
-      // store groups advance uniformly.
-      static_assert(kEpiWarps == 4, "one staging ring per epilogue warp and TMEM lane quarter");
-      constexpr int kBoxC = CTB_TM_EPI_BOX_C;
-      constexpr int kChunksPerBox = kBoxC / 32;
-      static_assert(kBoxC == 32 || kBoxC == 64, "box channels");
-      static_assert(BN % kBoxC == 0, "boxes per tile");
-      constexpr int kBoxes = BN / kBoxC;
-      constexpr int kBufs = kSlots / kChunksPerBox;
-      constexpr int kAheadU = kLoadAhead / kChunksPerBox > 0 ? kLoadAhead / kChunksPerBox : 1;
-      static_assert(kAheadU < kBufs, "residual look-ahead below the buffer count");
-      constexpr int kBufFloats = kBoxC * 32;
-      float* ring = staging + quarter * (kSlots * 32 * 32);
-      uint64_t* buf_bar = &bars->residual_full[quarter * kSlots];
-      const int total_units = my_tiles * kBoxes;
-      struct WarpSpan {
-        int hw0, img, valid;
-        bool one_image;
-      };
-      auto warp_span = [&](long long tile) {
-        const long long mt = tile / co_tiles;
-        const int rows = tile_rows(mt);
-        const int first = quarter * 32;
-        WarpSpan s{0, 0, max(0, min(32, rows - first)), false};
-        if (s.valid == 0) return s;
-        const long long p0 = tile_p0(mt) + first;
-        const long long img = p0 / pixels_per_image;
-        s.img = static_cast<int>(img);
-        s.hw0 = static_cast<int>(p0 - img * pixels_per_image);
-        s.one_image = s.valid == 32 && s.hw0 + 32 <= pixels_per_image;
-        return s;
-      };
-      auto issue_residual = [&](int u) {
-        if (kEpilogue != kBatchNormAddRelu || u >= total_units || lane != 0) return;
-        const int b = u % kBufs;
-        const long long tile = tile_index(u / kBoxes);
-        const WarpSpan s = warp_span(tile);
-        const int ch0 = static_cast<int>(tile % co_tiles) * BN + kBoxC * (u % kBoxes);
-        if (s.one_image && ch0 < p.k) {
-          mbar_arrive_expect_tx(&buf_bar[b], kBufFloats * 4u);
-          tma_load_3d(ring + b * kBufFloats, tma_res, &buf_bar[b], s.hw0, ch0, s.img);
-        } else {
-          mbar_arrive(&buf_bar[b]);  // read with plain loads when the unit runs
-        }
-      };
-      for (int u = 0; u < kAheadU; ++u) issue_residual(u);
-      int local = 0;
-      for (; local < my_tiles; ++local) {
-        const int buf = local % T::kAccBufs;
-        const long long tile = tile_index(local);
-        const int co0 = static_cast<int>(tile % co_tiles) * BN;
-        const WarpSpan span = warp_span(tile);
-        load_params(co0);
-        const bool ready = mbar_wait(&bars->tmem_full[buf], (local / T::kAccBufs) & 1, abort, scratch, 37);
-        // The four warps leave together (the abort is decided per tile).
-        if (epilogue_any(0, !ready)) break;
-        tc_fence_after_sync();
-        const uint32_t taddr = tmem + buf * T::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
-        // Plain-path addressing of this lane's pixel (output offset of channel 0).
-        long long px_base = -1;
-        if (!span.one_image && lane < span.valid) {
-          const long long pixel = tile_p0(tile / co_tiles) + quarter * 32 + lane;
-          const long long img = pixel / pixels_per_image;
-          px_base = img * p.k * pixels_per_image + (pixel - img * pixels_per_image);
-        }
-#pragma unroll
-        for (int bx = 0; bx < kBoxes; ++bx) {
-          const int u = local * kBoxes + bx;
-          const int b = u % kBufs;
-          const int box_ch0 = co0 + kBoxC * bx;
-          const bool boxed = span.one_image && box_ch0 < p.k;
-          if (kEpilogue == kBatchNormAddRelu) {
-            // A timeout is recorded (abort); the warps still leave together
-            // at the next tile.
-            mbar_wait(&buf_bar[b], (u / kBufs) & 1, abort, scratch, 38);
-          }
-#pragma unroll
-          for (int cc = 0; cc < kChunksPerBox; ++cc) {
-            const int ci = bx * kChunksPerBox + cc;
-            const int ch0 = co0 + 32 * ci;
-            float* cell = ring + b * kBufFloats + cc * 1024 + lane;  // [channel j][pixel lane] = cell[32 j]
-            uint32_t v[32];
-            load_acc(taddr, ci, v);
-            const int rows = min(32, p.k - ch0);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float xv = __uint_as_float(v[j]);
-              if (kEpilogue != kPlain) {
-                xv = (xv - __shfl_sync(0xffffffffu, pm[ci], j)) * __shfl_sync(0xffffffffu, pa[ci], j) +
-                     __shfl_sync(0xffffffffu, pb[ci], j);
-              }
-              if (boxed) {
-                if (kEpilogue == kBatchNormAddRelu) xv += cell[32 * j];
-                if (kEpilogue == kBatchNormRelu || kEpilogue == kBatchNormAddRelu) xv = fmaxf(xv, 0.0f);
-                cell[32 * j] = xv;
-              } else {
-                const long long at = px_base + static_cast<long long>(ch0 + j) * pixels_per_image;
-                const bool in = px_base >= 0 && j < rows;
-                if (kEpilogue == kBatchNormAddRelu && in) xv += __ldg(residual + at);
-                if (kEpilogue == kBatchNormRelu || kEpilogue == kBatchNormAddRelu) xv = fmaxf(xv, 0.0f);
-                if (in) out[at] = xv;
-              }
-            }
-          }
-          if (boxed) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) {
-              asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-                               reinterpret_cast<uint64_t>(tma_out)),
-                           "r"(smem_addr(ring + b * kBufFloats)), "r"(span.hw0), "r"(box_ch0), "r"(span.img)
-                           : "memory");
-            }
-          }
-          if (lane == 0) {
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-            // The store of unit u + kAheadU - kBufs (the buffer's previous
-            // user) has been read out of shared memory.
-            asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kBufs - kAheadU) : "memory");
-          }
-          __syncwarp();
-          issue_residual(u + kAheadU);
-        }
-        // Hand the accumulator back to the issuer.
-        tc_fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->tmem_empty[buf]);
-      }
-      if (lane == 0) {
-        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-        if (kEpilogue == kBatchNormAddRelu) {
-          // Residual copies issued for units that were not reached (abort)
-          // must land before the CTA's shared memory is released.
-          const int issued = min(total_units, local * kBoxes + kAheadU);
-          for (int u = local * kBoxes; u < issued; ++u) {
-            volatile int never = 0;
-            mbar_wait(&buf_bar[u % kBufs], (u / kBufs) & 1, &never, scratch, 39);
-          }
         }
       }
     } else if (CTB_TM_A_TMA) {

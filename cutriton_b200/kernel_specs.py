@@ -116,41 +116,35 @@ def _conv_specs() -> list[KernelSpec]:
     def tm_smem(n128: int, n64: int, slots: int, a_ring: int) -> int:
         # weight stages + barriers + k-chunk table + epilogue staging ring +
         # activation ring + alignment slack
-        return max(n128 * 32768, n64 * 16384) + 640 + 1024 + slots * 16384 + a_ring * 16384 + 1024
+        return max(n128 * 32768, n64 * 16384) + 512 + 1024 + slots * 16384 + a_ring * 16384 + 1024
 
-    def tm_defines(n128: int, n64: int, slots: int, ahead: int, a_tma: int, epi_mode: int = 0, box_c: int = 64,
-                   a_quarter: int = 0) -> dict[str, str]:
+    def tm_defines(n128: int, n64: int, slots: int, ahead: int, a_tma: int) -> dict[str, str]:
         return {"CTB_TM_STAGES_N128": str(n128), "CTB_TM_STAGES_N64": str(n64), "CTB_TM_SLOTS": str(slots),
                 "CTB_TM_LOAD_AHEAD": str(ahead), "CTB_TM_A_TMA": str(a_tma), "CTB_TM_IMAGE_TILES": "0",
                 # One gather group with two epilogue halves (CTB_TM_EPI_WARPS=8) was
                 # measured slower for the 1x1 variant too: the gather limits it.
-                "CTB_TM_GATHER_GROUPS": "2", "CTB_TM_EPI_WARPS": "4", "CTB_TM_SPLIT_N": "1",
-                "CTB_TM_EPI_MODE": str(epi_mode), "CTB_TM_EPI_BOX_C": str(box_c),
-                "CTB_TM_A_QUARTER": str(a_quarter)}
-
-    def boxes(epi_mode: int, box_c: int, a_quarter: int) -> dict:
-        """Tensor-map boxes the epilogue / activation modes copy."""
-        out_box = [128, 32, 1] if epi_mode == 0 else [32, box_c, 1]
-        return {"tma_out": {"box": out_box}, "tma_res": {"box": out_box},
-                "tma_x": {"box": [32, 32, 1] if a_quarter else [128, 32, 1]}}
+                "CTB_TM_GATHER_GROUPS": "2", "CTB_TM_EPI_WARPS": "4", "CTB_TM_SPLIT_N": "1"}
 
     # Epilogue tensor copies over the [N][K][H*W] view (optional: bound as
     # zeros when H*W*4 is not a multiple of 16; the kernel then stores from
     # registers). tma_x: activation blocks of the 1x1 variant.
-    # Each epilogue warp stores / loads its own {32 pixels, 32 channels} box.
-    tma_out = arg("tma_out", "tensormap", "tensor_map", tensor="output", index=0, box=[32, 32, 1], merge_inner=2,
+    tma_out = arg("tma_out", "tensormap", "tensor_map", tensor="output", index=0, box=[128, 32, 1], merge_inner=2,
                   optional=1)
-    tma_res = arg("tma_res", "tensormap", "tensor_map", tensor="input", index=6, box=[32, 32, 1], merge_inner=2,
+    tma_res = arg("tma_res", "tensormap", "tensor_map", tensor="input", index=6, box=[128, 32, 1], merge_inner=2,
                   optional=1)
-    tma_x = arg("tma_x", "tensormap", "tensor_map", tensor="input", index=0, box=[32, 32, 1], merge_inner=2,
+    tma_x = arg("tma_x", "tensormap", "tensor_map", tensor="input", index=0, box=[128, 32, 1], merge_inner=2,
                 optional=1)
     one_by_one = (
         {"kind": "dim_le", "source": "input", "index": 1, "axis": 2, "value": 1},
         {"kind": "dim_le", "source": "input", "index": 1, "axis": 3, "value": 1},
         {"kind": "attribute_list_eq", "name": "strides", "value": [1, 1], "default": [1, 1]},
         {"kind": "attribute_list_eq", "name": "pads", "value": [0, 0, 0, 0], "default": [0, 0, 0, 0]},
-        # even H and W: H*W % 4 == 0, so every image-aligned tile moves by tensor copies
-        {"kind": "dim_multiple_of", "source": "output", "index": 0, "axis": 2, "value": 2},
+        # H a multiple of 4 and W even (the 56x56 and 28x28 layers): H*W % 4 == 0, so every
+        # image-aligned tile moves by tensor copies. At 14x14 two of three 128-pixel tiles
+        # straddle two images and fall back to global loads anyway; there the general
+        # sibling was measured 17 % faster (256->1024, 1024->256 and 1024->512 at N=256),
+        # so those layers lower to it.
+        {"kind": "dim_multiple_of", "source": "output", "index": 0, "axis": 2, "value": 4},
         {"kind": "dim_multiple_of", "source": "output", "index": 0, "axis": 3, "value": 2},
     )
     # Input windows of the small-channel variant: box {232 columns, 11 rows,
@@ -163,28 +157,22 @@ def _conv_specs() -> list[KernelSpec]:
         maps = ((tma_w64, tma_out) + ((tma_res,) if op_type.endswith("AddRelu") else ()) + (tma_x,)
                 + ((tma_xwin,) if with_window else ()))
         overrides = tiny_box if with_window else {}
-        res = op_type.endswith("AddRelu")
-        arg_names = {a.name for a in maps + arguments[1:]}
-        variants = []
-        for tag, em, bc, aq in (("", 0, 64, 0), ("_ew32", 1, 32, 0), ("_ew64", 1, 64, 0), ("_ew64q", 1, 64, 1)):
-            ov = {k: v for k, v in {**overrides, **boxes(em, bc, aq)}.items() if k in arg_names}
-            if not aq:
-                # Any shape: activations gathered with global loads.
-                variants.append(Variant(
-                    "persistent_m128n128k32_tmem_a_3xtf32" + tag, num_warps=14,
-                    shared_memory_bytes=tm_smem(3, 6, 4, 0), defines=tm_defines(3, 6, 4, 2, 0, em, bc, aq),
-                    meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, arg_overrides=ov))
+        variants = [
+            # Any shape: activations gathered with global loads.
+            Variant("persistent_m128n128k32_tmem_a_3xtf32", num_warps=14,
+                    shared_memory_bytes=tm_smem(3, 6, 4, 0), defines=tm_defines(3, 6, 4, 2, 0),
+                    meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, arg_overrides=overrides),
             # 1x1 / stride 1 / no padding: activation blocks by TMA. With a
             # residual, the epilogue's residual stream limits these layers: one
             # weight stage less for a 5-slot staging ring loading 3 chunks ahead
             # (measured 4-7.5 % faster on the ResNet shapes; 4.6 % slower without
             # a residual, so only for this family).
-            variants.append(Variant(
-                "persistent_m128n128k32_tmem_a_3xtf32_1x1tma" + tag, num_warps=14,
-                shared_memory_bytes=tm_smem(2, 5, 5, 4) if res else tm_smem(3, 5, 4, 4),
-                defines=tm_defines(2, 5, 5, 3, 1, em, bc, aq) if res else tm_defines(3, 5, 4, 2, 1, em, bc, aq),
-                meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, constraints=one_by_one, default=(tag == ""),
-                arg_overrides=ov))
+            Variant("persistent_m128n128k32_tmem_a_3xtf32_1x1tma", num_warps=14,
+                    shared_memory_bytes=tm_smem(2, 5, 5, 4) if op_type.endswith("AddRelu") else tm_smem(3, 5, 4, 4),
+                    defines=tm_defines(2, 5, 5, 3, 1) if op_type.endswith("AddRelu") else tm_defines(3, 5, 4, 2, 1),
+                    meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128}, constraints=one_by_one, default=True,
+                    arg_overrides=overrides),
+        ]
         if with_window:
             # C <= 4 (the stem): listed first so it leads when the 1x1 default does not apply.
             variants.insert(0, Variant(
@@ -192,10 +180,7 @@ def _conv_specs() -> list[KernelSpec]:
                 shared_memory_bytes=tm_smem(2, 4, 4, 0) + window_bytes,
                 defines={**tm_defines(2, 4, 4, 2, 0), "CTB_TM_WINDOW": "1"},
                 meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128},
-                constraints=({"kind": "dim_le", "source": "input", "index": 1, "axis": 1, "value": 4},),
-                # Its own window map keeps the full box (the tiny box is for the
-                # variants that never load a window).
-                arg_overrides={k: v for k, v in boxes(0, 64, 0).items() if k in arg_names}))
+                constraints=({"kind": "dim_le", "source": "input", "index": 1, "axis": 1, "value": 4},)))
         specs.append(KernelSpec(
             kernel_id=kernel_id.replace("tcgen05", "tcgen05_tmem"), op_type=op_type, version=1,
             source="conv_tm.cu", symbol=symbol.replace("_tc", "_tm"),
@@ -440,7 +425,7 @@ def _gemm_specs() -> list[KernelSpec]:
     ) + RESERVED
     fp32_tm_grid = ({"kind": "min", "args": [mul(ceil_div(out_dim(0), literal(128)), ceil_div(out_dim(1), literal(128))),
                                              {"kind": "sm_count"}]},)
-    fp32_tm_smem = 3 * 32768 + 640 + 1024 + 4 * 16384 + 1024
+    fp32_tm_smem = 3 * 32768 + 512 + 1024 + 4 * 16384 + 1024
     fp32_tm = KernelSpec(
         kernel_id="gemm.fp32.tcgen05_tmem", op_type="Gemm", version=1, source="conv_tm.cu", symbol="ctb_conv_f32_tm",
         arguments=fp32_tm_args, grid=fp32_tm_grid,
