@@ -59,6 +59,9 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--tuning", choices=["TuneOnMiss", "Disabled"], default="TuneOnMiss",
                    help="ResNet-50 candidate selection: tuned during warm-up into a per-run cache (default, "
                         "as a deployment tunes once and then runs from the cache) or the pack defaults")
+    p.add_argument("--tuning-cache", default=None,
+                   help="tuning cache directory (default: a fresh one per run); a run with a filled cache "
+                        "reads its choices instead of timing candidates")
     p.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
                    help="run one small kernel case three times (for ncu captures) and exit")
     p.add_argument("--config", type=int, choices=[2, 3, 4],
@@ -562,7 +565,8 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
     # caches the choice; every later engine and context of this run reads it.
     import tempfile
 
-    tuning_dir = tempfile.mkdtemp(prefix=f"ctb_bench_tuning_{rank}_")
+    tuning_dir = (os.path.join(args.tuning_cache, f"rank{rank}") if args.tuning_cache
+                  else tempfile.mkdtemp(prefix=f"ctb_bench_tuning_{rank}_"))
     tuning = dict(tuning_mode=ct.TUNING_TUNE_ON_MISS if args.tuning == "TuneOnMiss" else ct.TUNING_DISABLED,
                   tuning_cache_dir=tuning_dir)
     engine = ct.build_engine(model, device_id=local, enable_cuda_graph=True, enable_profiling=False,
