@@ -362,6 +362,26 @@ def run_config3(args, peaks) -> dict:
             "layers": rows}
 
 
+def bench_tuning(args, rank: int) -> dict:
+    """Engine options for the candidate choice of every timed engine:
+    TuneOnMiss times every numerically valid candidate of each op on its
+    first run (a warm-up, outside the timed region) and caches the choice in
+    this rank's cache directory, which every later engine of the run reads."""
+    import tempfile
+
+    import cutriton_b200 as ct
+
+    tuning_dir = (os.path.join(args.tuning_cache, f"rank{rank}") if args.tuning_cache
+                  else tempfile.mkdtemp(prefix=f"ctb_bench_tuning_{rank}_"))
+    return dict(tuning_mode=ct.TUNING_TUNE_ON_MISS if args.tuning == "TuneOnMiss" else ct.TUNING_DISABLED,
+                tuning_cache_dir=tuning_dir)
+
+
+def chosen_kernels(engine, ctx) -> list[str]:
+    """Kernel (candidate id without the backend prefix) each op runs."""
+    return [op["candidates"][ctx.selected_candidate(i)].split(":", 1)[-1] for i, op in enumerate(engine.ops())]
+
+
 def run_config4(args, world, rank, local, peaks, peak_kind) -> dict:
     """Config 4: FFN H=1024, I=4096, global M=65536 split over the ranks (no collective)."""
     import torch
@@ -372,20 +392,21 @@ def run_config4(args, world, rank, local, peaks, peak_kind) -> dict:
     m_rank = global_m // world
     w = workloads.ffn_weights(h, i, seed=0)
     engine = ct.build_engine(workloads.build_ffn(w, m_rank, h, i), device_id=local, enable_cuda_graph=True,
-                             tuning_mode=ct.TUNING_DISABLED)
+                             **bench_tuning(args, rank))
     ctx = engine.create_context()
     x = torch.from_numpy(workloads.ffn_input(m_rank, h, seed=rank)).cuda(local)
     y = torch.empty(m_rank, h, dtype=torch.float16, device=f"cuda:{local}")
     ctx.bind_tensor("x", x)
     ctx.bind_tensor("output", y, output=True)
     times = time_context(ctx, torch.cuda.Stream(local), args.steps, args.warmup, all_times=True)
+    kernels = chosen_kernels(engine, ctx)
     ms = max_over_ranks(float(np.median(times)), world)
     p95 = max_over_ranks(float(np.percentile(times, 95)), world)
     flops = 4.0 * h * i * global_m
     tflops = flops / ms / 1e9
     return {"metric": "FFN FP16 tokens/s (config 4: H=1024, I=4096, global M=65536)", "unit": "tokens/s",
             "value": global_m / ms * 1e3, "ms_per_step": ms, "ms_p95": p95, "tflops": tflops,
-            "tflops_per_gpu": tflops / world, "roofline": ffn_roofline(tflops / world, peaks, peak_kind),
+            "tflops_per_gpu": tflops / world, "roofline": ffn_roofline(tflops / world, peaks, peak_kind, kernels),
             "rows_per_gpu": m_rank, "n_gpus": world, "scaling": "strong", "higher_is_better": True,
             "l2": "inputs larger than L2 at 1 GPU (M=65536: 128 MB in, 512 MB intermediate)"}
 
@@ -563,12 +584,7 @@ def run_resnet(args, world, rank, local, peaks, peak_kind) -> dict:
     # Candidate choice: TuneOnMiss times every numerically valid candidate of
     # each op on its first run (the warm-up, outside the timed region) and
     # caches the choice; every later engine and context of this run reads it.
-    import tempfile
-
-    tuning_dir = (os.path.join(args.tuning_cache, f"rank{rank}") if args.tuning_cache
-                  else tempfile.mkdtemp(prefix=f"ctb_bench_tuning_{rank}_"))
-    tuning = dict(tuning_mode=ct.TUNING_TUNE_ON_MISS if args.tuning == "TuneOnMiss" else ct.TUNING_DISABLED,
-                  tuning_cache_dir=tuning_dir)
+    tuning = bench_tuning(args, rank)
     engine = ct.build_engine(model, device_id=local, enable_cuda_graph=True, enable_profiling=False,
                              enable_residual_fusion=True, **tuning)
     ctx = engine.create_context()
@@ -729,7 +745,7 @@ def run_ffn(args, world, rank, local, peaks, peak_kind) -> dict:
     t, h, i = FFN["tokens"], FFN["hidden"], FFN["inner"]
     w = workloads.ffn_weights(h, i, seed=0)
     engine = ct.build_engine(workloads.build_ffn(w, t, h, i), device_id=local, enable_cuda_graph=True,
-                             enable_profiling=False, tuning_mode=ct.TUNING_DISABLED)
+                             enable_profiling=False, **bench_tuning(args, rank))
     ctx = engine.create_context()
     x = torch.from_numpy(workloads.ffn_input(t, h, seed=rank)).to(device)
     y = torch.empty(t, h, dtype=torch.float16, device=device)
@@ -752,22 +768,23 @@ def run_ffn(args, world, rank, local, peaks, peak_kind) -> dict:
             e.record(stream)
             ctx.synchronize()
             times.append(s.elapsed_time(e))
+    kernels = chosen_kernels(engine, ctx)
     med = max_over_ranks(float(np.median(times)), world)
     p95 = max_over_ranks(float(np.percentile(times, 95)), world)
     flops = 4.0 * t * h * i
     tflops = flops / (med / 1e3) / 1e12
     return {"metric": "FFN FP16 tokens/s (M=4096, H=768, I=3072)", "value": world * t / (med / 1e3),
             "unit": "tokens/s", "ms_per_step": med, "ms_p95": p95, "tflops": tflops,
-            "roofline": ffn_roofline(tflops, peaks, peak_kind),
+            "roofline": ffn_roofline(tflops, peaks, peak_kind, kernels),
             "scaling": "weak (config 1 per rank)", "l2": "flushed (256 MB write) before every timed step",
             "input": x.cpu().numpy(), "output": y.cpu().numpy(), "weights": w}
 
 
-def ffn_roofline(tflops: float, peaks: dict, peak_kind: str) -> dict:
+def ffn_roofline(tflops: float, peaks: dict, peak_kind: str, kernels: list[str]) -> dict:
     """FFN block (GemmGelu + Gemm + SkipLayerNorm) against the FP16 tensor
     peak: 4*H*I FLOPs per token; the kernels run well under a millisecond at
     full clock, so the burst BF16 figure (= FP16 rate) is the basis."""
-    return {"bound": "tensor", "kernel": "FFN block: ctb_gemm_gelu_f16_tp + ctb_gemm_f16_tp + ctb_skip_layer_norm_f16",
+    return {"bound": "tensor", "kernel": "FFN block: " + " + ".join(kernels),
             "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
             "frac": tflops / peaks["bf16_tflops"], "peak_basis": f"{peak_kind} bf16_tflops (burst)"}
 

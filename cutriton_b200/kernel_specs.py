@@ -383,6 +383,26 @@ def _gemm_specs() -> list[KernelSpec]:
                                         {"kind": "sm_count"}]},)
     tp_variant = Variant("persistent_m128n256k64_2acc", num_warps=18, shared_memory_bytes=196608 + 32768 + 256 + 1024,
                          meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=True)
+    # CTA pairs (clusters of two SMs, tcgen05 cta_group::2): 2 x min(#256x128
+    # pair tiles, #SMs / 2) CTAs. The kernel picks 256-, 192- or 128-wide
+    # tiles at run time; each CTA reads its half of B^T through the map of
+    # that half width.
+    literal = lambda v: {"kind": "literal", "value": v}  # noqa: E731
+    pair_args = (
+        arg("tma_a", "tensormap", "tensor_map", tensor="input", index=0, box=[64, 128], swizzle=128),
+        *(arg(f"tma_b{rows}", "tensormap", "tensor_map", tensor="input", index=1, box=[64, rows], swizzle=128,
+              prepack="transpose_2d") for rows in (128, 96, 64)),
+        arg("tma_out", "tensormap", "tensor_map", tensor="output", index=0, box=[32, 32], swizzle=64, optional=1),
+        arg("output", "*fp16", "output", index=0),
+        arg("m", "i32", "output_dim", index=0, axis=0),
+        arg("n", "i32", "output_dim", index=0, axis=1),
+        arg("k", "i32", "input_dim", index=0, axis=1),
+    ) + RESERVED
+    pair_grid = (mul(literal(2), {"kind": "min", "args": [
+        mul(ceil_div(out_dim(0), literal(256)), ceil_div(out_dim(1), literal(128))),
+        ceil_div({"kind": "sm_count"}, literal(2))]}),)
+    pair_variant = Variant("pair_m256n256k64_2acc", num_warps=18, shared_memory_bytes=196608 + 32768 + 256 + 1024,
+                           meta={"BLOCK_M": 256, "BLOCK_N": 128})
     tc = [
         KernelSpec(kernel_id="gemm.fp16.tcgen05_persistent", op_type="Gemm", version=1, source="gemm_f16_tp.cu",
                    symbol="ctb_gemm_f16_tp", arguments=tp_args, grid=tp_grid, dtype="float16",
@@ -390,6 +410,12 @@ def _gemm_specs() -> list[KernelSpec]:
         KernelSpec(kernel_id="gemm_gelu.fp16.tcgen05_persistent", op_type="GemmGelu", version=1,
                    source="gemm_f16_tp.cu", symbol="ctb_gemm_gelu_f16_tp", arguments=tp_args, grid=tp_grid,
                    dtype="float16", constraints=tc_constraints, variants=(tp_variant,)),
+        KernelSpec(kernel_id="gemm.fp16.tcgen05_pair", op_type="Gemm", version=1, source="gemm_f16_2sm.cu",
+                   symbol="ctb_gemm_f16_2sm", arguments=pair_args, grid=pair_grid, dtype="float16",
+                   constraints=tc_constraints, variants=(pair_variant,)),
+        KernelSpec(kernel_id="gemm_gelu.fp16.tcgen05_pair", op_type="GemmGelu", version=1,
+                   source="gemm_f16_2sm.cu", symbol="ctb_gemm_gelu_f16_2sm", arguments=pair_args, grid=pair_grid,
+                   dtype="float16", constraints=tc_constraints, variants=(pair_variant,)),
         KernelSpec(kernel_id="gemm.fp16.tcgen05", op_type="Gemm", version=1, source="gemm_f16_tc.cu",
                    symbol="ctb_gemm_f16_tc", arguments=tc_args(128), grid=grid, dtype="float16",
                    constraints=tc_constraints, variants=tc_variants()),

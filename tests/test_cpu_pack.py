@@ -155,7 +155,7 @@ def test_pack_entries_are_cubins_for_sm100():
 def _kernel_constant(source: str, name: str) -> int:
     import re
 
-    match = re.search(rf"constexpr int {name} = (\d+);", source)
+    match = re.search(rf"constexpr (?:int|uint32_t) {name} = (\d+)u?;", source)
     assert match, f"{name} not found"
     return int(match.group(1))
 
@@ -167,19 +167,29 @@ def test_launch_shapes_match_the_kernels():
     from cutriton_b200.kernel_sdk import _variant_arguments
 
     kernels = Path(kernel_specs.__file__).resolve().parent / "csrc" / "kernels"
-    gemm = (kernels / "gemm_f16_tp.cu").read_text()
-    epilogue_warps = _kernel_constant(gemm, "kEpilogueWarps")
-    chunk = _kernel_constant(gemm, "kChunk")
     checked = set()
     for spec in kernel_specs.all_specs():
         for variant in spec.variants:
             args = {a["name"]: a["source"] for a in _variant_arguments(spec, variant)}
-            if spec.source == "gemm_f16_tp.cu":
+            if spec.source in ("gemm_f16_tp.cu", "gemm_f16_2sm.cu"):
+                gemm = (kernels / spec.source).read_text()
+                epilogue_warps = _kernel_constant(gemm, "kEpilogueWarps")
+                chunk = _kernel_constant(gemm, "kChunk")
                 # producer + issuer + epilogue warps; 32 x chunk FP16 store box, swizzle = its row bytes
                 assert variant.num_warps == 2 + epilogue_warps, spec.kernel_id
                 assert args["tma_out"]["box"] == [chunk, 32], spec.kernel_id
                 assert args["tma_out"]["swizzle"] == 2 * chunk, spec.kernel_id
+                # stage ring + store staging + barriers + 1 KB alignment slack
+                ring = _kernel_constant(gemm, "kRingBytes")
+                need = ring + epilogue_warps * 32 * chunk * 2 + 1024
+                assert need < variant.shared_memory_bytes <= 232448, spec.kernel_id
                 checked.add(spec.source)
+            if spec.source == "gemm_f16_2sm.cu":
+                # A: 128 rows per CTA; B^T: half of each tile width (256, 192, 128) per CTA
+                assert args["tma_a"]["box"] == [64, 128], spec.kernel_id
+                for rows in (128, 96, 64):
+                    assert args[f"tma_b{rows}"]["box"] == [64, rows], spec.kernel_id
+                    assert args[f"tma_b{rows}"]["prepack"] == "transpose_2d", spec.kernel_id
             if spec.source == "conv_tm.cu":
                 d = variant.defines
                 warps = 2 + int(d["CTB_TM_EPI_WARPS"]) + 4 * int(d["CTB_TM_GATHER_GROUPS"])
@@ -193,7 +203,7 @@ def test_launch_shapes_match_the_kernels():
                     need += 2 * 232 * 11 * 4 * 4
                 assert need <= variant.shared_memory_bytes <= 232448, (spec.kernel_id, variant.variant_id)
                 checked.add(spec.source)
-    assert checked == {"gemm_f16_tp.cu", "conv_tm.cu"}
+    assert checked == {"gemm_f16_tp.cu", "gemm_f16_2sm.cu", "conv_tm.cu"}
 
 
 def test_window_variant_keeps_its_full_window_box():
