@@ -13,7 +13,7 @@
 // Every wait is bounded: after kWaitLimitNs of global time the waiting thread
 // records kErrorWaitTimeout in the error block and reports failure, and the
 // kernel unwinds (drains what it issued, frees TMEM, returns) instead of
-// hanging. No cluster multicast is used anywhere.
+// hanging. Every tensor copy fills the shared memory of the CTA that issues it.
 #pragma once
 
 #include "common.cuh"
