@@ -198,6 +198,16 @@ def _bandwidth_cases():
     ]
 
 
+def _gemm_f16_case(m: int, n: int, k: int, kernel_id: str):
+    """One FP16 Gemm node (B constant) with candidate `kernel_id` selected."""
+    rng = np.random.default_rng(0)
+    b = (rng.standard_normal((k, n)) * 0.02).astype(np.float16)
+    e, ctx, keep = _single_op_case("Gemm", [("a", [m, k])], [m, n], dtype="float16", constants={"b": b})
+    ids = [c.split(":")[1] for c in e.ops()[0]["candidates"]]
+    ctx.select_candidate(0, ids.index(kernel_id))
+    return e, ctx, keep
+
+
 def _resnet_case(batch: int):
     import torch
     import cutriton_b200 as ct
@@ -226,6 +236,9 @@ PROFILE_CASES = {
     "conv1x1_64to256_add_56x56_bs64": lambda: _conv_case(64, 64, 56, 256, 1, 1, 0, residual=True),
     "stem7x7_bs64": lambda: _conv_case(64, 3, 224, 64, 7, 2, 3),
     "ffn_4096x768x3072": _ffn_case,
+    # FFN config-4 down-projection shape at M=16384 (A 134 MB): CTA pair vs single CTA.
+    "gemm_f16_pair_16384x1024x4096": lambda: _gemm_f16_case(16384, 1024, 4096, "gemm.fp16.tcgen05_pair"),
+    "gemm_f16_tp_16384x1024x4096": lambda: _gemm_f16_case(16384, 1024, 4096, "gemm.fp16.tcgen05_persistent"),
     "bandwidth_ops": None,
     "resnet50_bs32": lambda: _resnet_case(32),
     "resnet50_bs64": lambda: _resnet_case(64),
