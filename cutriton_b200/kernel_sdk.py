@@ -86,6 +86,10 @@ class Variant:
     # Per-variant argument overrides (e.g. tensor-map boxes), by arg name.
     arg_overrides: dict[str, dict[str, Any]] = field(default_factory=dict)
     constraints: tuple[dict[str, Any], ...] = ()
+    # Launch with programmatic stream serialisation: the kernel's CTAs may
+    # start (and run their prologue up to CTB_GRID_DEPENDENCY_SYNC) on SMs the
+    # preceding kernel has left, before that kernel has finished.
+    programmatic_launch: bool = False
 
 
 @dataclass(frozen=True)
@@ -248,10 +252,10 @@ def build_pack(output: Path, compile_cubin: Callable[[Path, Path, dict[str, str]
             "min_compute_capability": spec.min_compute_capability,
             "num_warps": variant.num_warps,
             "num_stages": 1,
-            # Every kernel supports it (CTB_GRID_DEPENDENCY_SYNC), but overlapping
-            # the persistent kernels measured slower on ResNet-50 (21.3 vs
-            # 19.0 ms/step), so the pack does not request it.
-            "programmatic_launch": 0,
+            # Every kernel supports it (CTB_GRID_DEPENDENCY_SYNC); a variant
+            # asks for it. Overlapping the persistent conv kernels measured
+            # slower on ResNet-50 (21.3 vs 19.0 ms/step), so those do not.
+            "programmatic_launch": int(variant.programmatic_launch),
             "shared_memory_bytes": variant.shared_memory_bytes,
             "arguments": _variant_arguments(spec, variant),
             "grid": _padded_grid(spec.grid),

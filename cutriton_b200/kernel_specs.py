@@ -382,12 +382,11 @@ def _gemm_specs() -> list[KernelSpec]:
     tp_grid = ({"kind": "min", "args": [mul(ceil_div(out_dim(0), meta("BLOCK_M")), ceil_div(out_dim(1), meta("BLOCK_N"))),
                                         {"kind": "sm_count"}]},)
     tp_variant = Variant("persistent_m128n256k64_2acc", num_warps=18, shared_memory_bytes=196608 + 32768 + 256 + 1024,
-                         meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=True)
+                         meta={"BLOCK_M": 128, "BLOCK_N": 128}, default=True, programmatic_launch=True)
     # CTA pairs (clusters of two SMs, tcgen05 cta_group::2): 2 x min(#256x128
     # pair tiles, #SMs / 2) CTAs. The kernel picks 256-, 192- or 128-wide
     # tiles at run time; each CTA reads its half of B^T through the map of
     # that half width.
-    literal = lambda v: {"kind": "literal", "value": v}  # noqa: E731
     pair_args = (
         arg("tma_a", "tensormap", "tensor_map", tensor="input", index=0, box=[64, 128], swizzle=128),
         *(arg(f"tma_b{rows}", "tensormap", "tensor_map", tensor="input", index=1, box=[64, rows], swizzle=128,
@@ -402,7 +401,7 @@ def _gemm_specs() -> list[KernelSpec]:
         mul(ceil_div(out_dim(0), literal(256)), ceil_div(out_dim(1), literal(128))),
         ceil_div({"kind": "sm_count"}, literal(2))]}),)
     pair_variant = Variant("pair_m256n256k64_2acc", num_warps=18, shared_memory_bytes=196608 + 32768 + 256 + 1024,
-                           meta={"BLOCK_M": 256, "BLOCK_N": 128})
+                           meta={"BLOCK_M": 256, "BLOCK_N": 128}, programmatic_launch=True)
     tc = [
         KernelSpec(kernel_id="gemm.fp16.tcgen05_persistent", op_type="Gemm", version=1, source="gemm_f16_tp.cu",
                    symbol="ctb_gemm_f16_tp", arguments=tp_args, grid=tp_grid, dtype="float16",
@@ -517,7 +516,9 @@ def _norm_specs() -> list[KernelSpec]:
                    dtype="float16", constraints=row_constraints(3), variants=variants),
         KernelSpec(kernel_id="skip_layer_norm.fp16.last_axis", op_type="SkipLayerNormalization", version=1,
                    source="norm.cu", symbol="ctb_skip_layer_norm_f16", arguments=norm_args(True), grid=grid,
-                   dtype="float16", constraints=row_constraints(4), variants=variants),
+                   dtype="float16", constraints=row_constraints(4),
+                   variants=(Variant("warp_per_row", num_warps=8, meta={"ROWS": 8}, default=True,
+                                     programmatic_launch=True),)),
         KernelSpec(kernel_id="softmax.fp16.last_axis", op_type="Softmax", version=1, source="norm.cu",
                    symbol="ctb_softmax_f16", arguments=softmax_args, grid=grid, dtype="float16",
                    constraints=row_constraints(None), variants=variants),
