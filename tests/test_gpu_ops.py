@@ -66,6 +66,8 @@ CONV_CASES = [
     (8, 64, 56, 56, 256, 1, 1, 0),    # > 2 persistent tiles per CTA (128-channel tiles)
     (8, 64, 56, 56, 64, 1, 1, 0),     # > 1 persistent tile per CTA (64-channel tiles)
     (2, 3, 224, 224, 64, 7, 2, 3),    # the ResNet stem: TMA input windows (small-channel variant)
+    (2, 3, 20, 20, 64, 7, 2, 3),      # C=3, tiles straddle images: dense-k global gather of that variant
+    (3, 1, 12, 12, 16, 3, 1, 1),      # C=1, one k block: dense-k global gather, K = 9
     (3, 64, 14, 14, 128, 1, 1, 0),    # 1x1 at 14x14: tiles straddle images, per-quarter TMA boxes
     (2, 128, 28, 28, 160, 1, 1, 0),   # 1x1 at 28x28, ragged channel tile (K = 160)
 ]
