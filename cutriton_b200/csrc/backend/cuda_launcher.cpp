@@ -193,7 +193,9 @@ Status EncodeTensorMap(const Tensor& tensor, const KernelArgumentSource& s, CUte
   CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE;
   if (s.swizzle_bytes == 32) swizzle = CU_TENSOR_MAP_SWIZZLE_32B;
   if (s.swizzle_bytes == 64) swizzle = CU_TENSOR_MAP_SWIZZLE_64B;
-  if (s.swizzle_bytes == 128) swizzle = CU_TENSOR_MAP_SWIZZLE_128B;
+  if (s.swizzle_bytes == 128) {
+    swizzle = s.swizzle_atom_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  }
   const CUresult result = drv::Get().cuTensorMapEncodeTiled(
       map, type, static_cast<cuuint32_t>(rank), address, dims, strides, box, element_strides,
       CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

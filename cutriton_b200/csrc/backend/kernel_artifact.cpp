@@ -196,6 +196,7 @@ KernelArgumentSpec ParseArgument(const json::Value& v) {
     s.map_output = tensor == "output";
     s.box = IntList(src.at("box"));
     s.swizzle_bytes = IntOr(src, "swizzle", 0);
+    s.swizzle_atom_bytes = static_cast<int>(IntOr(src, "swizzle_atom", 0));
     s.merge_inner = static_cast<int>(IntOr(src, "merge_inner", 1));
     s.optional = IntOr(src, "optional", 0) != 0;
     if (s.merge_inner < 1 || s.merge_inner > 4) throw std::runtime_error("tensor_map merge_inner must be 1..4");
@@ -206,6 +207,9 @@ KernelArgumentSpec ParseArgument(const json::Value& v) {
     if (s.swizzle_bytes != 0 && s.swizzle_bytes != 32 && s.swizzle_bytes != 64 &&
         s.swizzle_bytes != 128) {
       throw std::runtime_error("tensor_map swizzle must be 0, 32, 64 or 128");
+    }
+    if (s.swizzle_atom_bytes != 0 && (s.swizzle_atom_bytes != 32 || s.swizzle_bytes != 128)) {
+      throw std::runtime_error("tensor_map swizzle_atom must be 32 with a 128-byte swizzle");
     }
   }
   return arg;

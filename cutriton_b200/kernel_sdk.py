@@ -42,7 +42,7 @@ _SOURCE_FIELDS = {
     "attribute_f64": {"kind", "name", "alternate_name", "index", "default"},
     "literal_i32": {"kind", "default"},
     "runtime_reserved": {"kind"},
-    "tensor_map": {"kind", "tensor", "index", "box", "swizzle", "prepack", "merge_inner", "optional"},
+    "tensor_map": {"kind", "tensor", "index", "box", "swizzle", "swizzle_atom", "prepack", "merge_inner", "optional"},
 }
 _CONSTRAINT_FIELDS = {
     "attribute_i64_eq": {"kind", "name", "value", "default"},
@@ -171,6 +171,8 @@ def _validate_source(kernel_id: str, name: str, source: dict[str, Any]) -> None:
             raise ValueError(f"{kernel_id}: tensor_map must name an input or output")
         if source.get("swizzle", 0) not in {0, 32, 64, 128}:
             raise ValueError(f"{kernel_id}: invalid tensor_map swizzle")
+        if source.get("swizzle_atom", 0) not in {0, 32} or (source.get("swizzle_atom") and source.get("swizzle") != 128):
+            raise ValueError(f"{kernel_id}: tensor_map swizzle_atom must be 32 with a 128-byte swizzle")
 
 
 def _validate_grid(kernel_id: str, node: dict[str, Any], depth: int) -> None:

@@ -197,7 +197,57 @@ def _conv_specs() -> list[KernelSpec]:
                               meta={"BLOCK_PIXELS": 128, "BLOCK_CHANNELS": 128},
                               defines={"CTB_STAGES": str(stages)}, default=False),),
         ))
+    specs.extend(_conv1x1_mn_specs(one_by_one))
     return specs
+
+
+def _conv1x1_mn_specs(one_by_one: tuple[dict[str, Any], ...]) -> list[KernelSpec]:
+    """1x1 / stride-1 / unpadded convolutions with the output channels on M
+    (conv1x1_mn.cu): activations and results move as {32 px, 32 channel}
+    boxes of the [N][C][H*W] view, no gather. Candidates next to the TMEM
+    kernel; the tuner picks per layer."""
+    box = dict(box=[32, 32, 1], swizzle=128, merge_inner=2, optional=1)
+    w = arg("tma_w", "tensormap", "tensor_map", tensor="input", index=1, box=[32, 128, 1], swizzle=128,
+            prepack="conv_w_tf32x2_cb")
+    # X is the MN-major TF32 operand: 32-byte swizzle atoms (the tensor core's only layout for it).
+    maps = (w, arg("tma_x", "tensormap", "tensor_map", tensor="input", index=0, swizzle_atom=32, **box),
+            arg("tma_out", "tensormap", "tensor_map", tensor="output", index=0, **box))
+    res_map = arg("tma_res", "tensormap", "tensor_map", tensor="input", index=6, **box)
+    x = (arg("x", "*fp32", "input", index=0),)
+    out = (arg("output", "*fp32", "output", index=0),)
+    dims = (arg("n", "i32", "input_dim", index=0, axis=0), arg("c", "i32", "input_dim", index=0, axis=1),
+            arg("h", "i32", "input_dim", index=0, axis=2), arg("w", "i32", "input_dim", index=0, axis=3),
+            arg("k", "i32", "input_dim", index=1, axis=0))
+    families = [
+        ("conv.fp32.nchw.tcgen05_mn", "Conv", "ctb_conv1x1_f32_mn", maps + x + out + dims + RESERVED),
+        ("conv_bn.fp32.nchw.tcgen05_mn", "FusedConvBatchNorm", "ctb_conv1x1_bn_f32_mn",
+         maps + x + BN_TENSORS + out + dims + (EPSILON,) + RESERVED),
+        ("conv_bn_relu.fp32.nchw.tcgen05_mn", "FusedConvBatchNormRelu", "ctb_conv1x1_bn_relu_f32_mn",
+         maps + x + BN_TENSORS + out + dims + (EPSILON,) + RESERVED),
+        ("conv_bn_add_relu.fp32.nchw.tcgen05_mn", "FusedConvBatchNormAddRelu", "ctb_conv1x1_bn_add_relu_f32_mn",
+         maps + (res_map,) + x + BN_TENSORS + (arg("residual", "*fp32", "input", index=6),) + out + dims
+         + (EPSILON,) + RESERVED),
+    ]
+    # 128 channels x 128 pixels of one image per tile; persistent.
+    tiles = mul(out_dim(0), mul(ceil_div(mul(out_dim(2), out_dim(3)), literal(128)),
+                                ceil_div(out_dim(1), literal(128))))
+    grid = ({"kind": "min", "args": [tiles, {"kind": "sm_count"}]},)
+    constraints = one_by_one + (
+        {"kind": "input_is_constant", "index": 1},
+        {"kind": "dim_multiple_of", "source": "input", "index": 0, "axis": 1, "value": 32},
+    )
+    def smem(op_type: str) -> int:
+        # Stages of W_hi, W_lo, X_hi, X_lo (64 KB each: two with a residual,
+        # three without) + four epilogue warps x {32 px, 32 channel} boxes
+        # (two output boxes, plus three residual slots) + barriers + slack.
+        residual = op_type.endswith("AddRelu")
+        return (2 if residual else 3) * 65536 + 4 * (5 if residual else 2) * 4096 + 256 + 1024
+
+    return [KernelSpec(kernel_id=kernel_id, op_type=op_type, version=1, source="conv1x1_mn.cu", symbol=symbol,
+                       arguments=arguments, grid=grid, layout="NCHW", constraints=constraints,
+                       variants=(Variant("persistent_co128px128k32_3xtf32", num_warps=10,
+                                         shared_memory_bytes=smem(op_type), meta={"BLOCK_PIXELS": 128}),))
+            for kernel_id, op_type, symbol, arguments in families]
 
 
 def _elementwise_specs() -> list[KernelSpec]:

@@ -58,10 +58,13 @@ struct KernelArgumentSource {
   // for the folded dimension. An optional map whose strides or base are not
   // 16-byte aligned, or that the driver cannot encode for this tensor, is
   // bound as all zeros instead of failing the launch (the kernel must not use
-  // it then).
+  // it then). swizzle_atom_bytes = 32 (with a 128-byte swizzle) permutes
+  // 32-byte instead of 16-byte chunks within each 128-byte row, the layout
+  // of MN-major TF32 tensor-core operands.
   bool map_output{false};
   std::vector<int64_t> box;
   int swizzle_bytes{0};
+  int swizzle_atom_bytes{0};
   int merge_inner{1};
   bool optional{false};
 };
