@@ -232,7 +232,12 @@ def _conv1x1_mn_specs(one_by_one: tuple[dict[str, Any], ...]) -> list[KernelSpec
     tiles = mul(out_dim(0), mul(ceil_div(mul(out_dim(2), out_dim(3)), literal(128)),
                                 ceil_div(out_dim(1), literal(128))))
     grid = ({"kind": "min", "args": [tiles, {"kind": "sm_count"}]},)
-    constraints = one_by_one + (
+    # 1x1 / stride 1 / unpadded (the first four of one_by_one), C a multiple
+    # of 32, H and W even (H*W % 4 == 0: 16-byte rows for the tensor maps;
+    # the 56x56, 28x28 and 14x14 layers).
+    constraints = one_by_one[:4] + (
+        {"kind": "dim_multiple_of", "source": "output", "index": 0, "axis": 2, "value": 2},
+        {"kind": "dim_multiple_of", "source": "output", "index": 0, "axis": 3, "value": 2},
         {"kind": "input_is_constant", "index": 1},
         {"kind": "dim_multiple_of", "source": "input", "index": 0, "axis": 1, "value": 32},
     )

@@ -206,6 +206,28 @@ def test_launch_shapes_match_the_kernels():
     assert checked == {"gemm_f16_tp.cu", "gemm_f16_2sm.cu", "conv_tm.cu"}
 
 
+def test_conv1x1_mn_shared_memory_matches_the_kernel():
+    """The output-channels-on-M 1x1 kernel: 10 warps, and shared memory for
+    its stages (three without a residual, two with one; 64 KB each) and the
+    epilogue boxes (two output boxes per warp, plus three residual slots)."""
+    from cutriton_b200 import kernel_specs
+
+    source = (Path(kernel_specs.__file__).resolve().parent / "csrc" / "kernels" / "conv1x1_mn.cu").read_text()
+    assert "kStages = kResidual ? 2 : 3" in source
+    assert _kernel_constant(source, "kMaxResSlots") == 3 and _kernel_constant(source, "kOutSlots") == 2
+    assert _kernel_constant(source, "kEpiWarps") == 4
+    specs = [s for s in kernel_specs.all_specs() if s.source == "conv1x1_mn.cu"]
+    assert len(specs) == 4
+    for spec in specs:
+        residual = spec.op_type.endswith("AddRelu")
+        stage = 2 * (128 * 32 * 4) + 2 * (4 * 32 * 32 * 4)  # W_hi, W_lo, X_hi, X_lo
+        epilogue = 4 * ((3 if residual else 0) + 2) * 32 * 32 * 4
+        need = (2 if residual else 3) * stage + epilogue + 1024
+        (variant,) = spec.variants
+        assert variant.num_warps == 10
+        assert need < variant.shared_memory_bytes <= 232448, spec.kernel_id
+
+
 def test_window_variant_keeps_its_full_window_box():
     """The stem's input-window variant loads {232 columns, 11 rows, 4
     channels, 1 image} per tile and waits for exactly that many bytes; the
