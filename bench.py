@@ -208,6 +208,14 @@ def _gemm_f16_case(m: int, n: int, k: int, kernel_id: str):
     return e, ctx, keep
 
 
+def _with_candidate(case, kernel_id: str):
+    """Selects the candidate of op 0 whose kernel id is `kernel_id`."""
+    e, ctx, keep = case
+    ids = [c.split(":")[1] for c in e.ops()[0]["candidates"]]
+    ctx.select_candidate(0, ids.index(kernel_id))
+    return e, ctx, keep
+
+
 def _resnet_case(batch: int):
     import torch
     import cutriton_b200 as ct
@@ -234,6 +242,8 @@ PROFILE_CASES = {
     "conv3x3_64ch_56x56_bs64": lambda: _conv_case(64, 64, 56, 64, 3, 1, 1),
     "conv1x1_256to64_56x56_bs64": lambda: _conv_case(64, 256, 56, 64, 1, 1, 0),
     "conv1x1_64to256_add_56x56_bs64": lambda: _conv_case(64, 64, 56, 256, 1, 1, 0, residual=True),
+    "conv1x1_mn_64to256_add_56x56_bs64": lambda: _with_candidate(
+        _conv_case(64, 64, 56, 256, 1, 1, 0, residual=True), "conv_bn_add_relu.fp32.nchw.tcgen05_mn"),
     "stem7x7_bs64": lambda: _conv_case(64, 3, 224, 64, 7, 2, 3),
     "ffn_4096x768x3072": _ffn_case,
     # FFN config-4 down-projection shape at M=16384 (A 134 MB): CTA pair vs single CTA.

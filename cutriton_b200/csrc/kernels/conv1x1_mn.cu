@@ -27,7 +27,7 @@
 // Warps (320 threads): 0 — TMA producer (W_hi, W_lo, four X boxes per
 // 32-channel k block); 1 — TMEM owner and MMA issuer; 2-5 — split warps;
 // 6-9 — epilogue, one per TMEM lane quarter (warp % 4), each with its own
-// residual ring (loaded two chunks ahead) and two output boxes. Two TMEM
+// residual ring (loaded three chunks ahead) and two output boxes. Two TMEM
 // accumulators (2 x 128 columns) let the epilogue of tile i overlap the MMAs
 // of tile i + 1. Every wait is bounded (tc_common.cuh).
 
@@ -50,8 +50,8 @@ constexpr uint32_t kWPlane = kBM * kBK * 4;  // 16 KB: W_hi or W_lo, K-major row
 constexpr uint32_t kBox = 32 * 32 * 4;        // 4 KB: {32 px, 32 channels}, 128-byte swizzle
 constexpr uint32_t kXBytes = (kBN / 32) * kBox;  // 16 KB: four pixel boxes of one k block
 constexpr uint32_t kStageBytes = 2 * kWPlane + 2 * kXBytes;
-constexpr int kMaxResSlots = 3;
-constexpr int kResAhead = 2;
+constexpr int kMaxResSlots = 4;
+constexpr int kResAhead = 3;
 constexpr int kOutSlots = 2;
 constexpr uint32_t kTmemCols = 2 * kBN;
 constexpr int kChunks = kBN / 32;  // 32-pixel chunks per tile
@@ -59,8 +59,9 @@ constexpr int kChunks = kBN / 32;  // 32-pixel chunks per tile
 enum Epilogue { kPlain = 0, kBatchNorm = 1, kBatchNormRelu = 2, kBatchNormAddRelu = 3 };
 
 // Stages and epilogue boxes per kernel: with a residual, each epilogue warp
-// keeps a 3-slot residual ring besides its two output boxes, which leaves
-// room for two 64 KB stages; without one, three stages fit.
+// keeps a 4-slot residual ring (loads three chunks ahead) besides its two
+// output boxes, which leaves room for two 64 KB stages; without one, three
+// stages fit.
 template <int kEpilogue>
 struct Config {
   static constexpr bool kResidual = kEpilogue == kBatchNormAddRelu;

@@ -244,9 +244,9 @@ def _conv1x1_mn_specs(one_by_one: tuple[dict[str, Any], ...]) -> list[KernelSpec
     def smem(op_type: str) -> int:
         # Stages of W_hi, W_lo, X_hi, X_lo (64 KB each: two with a residual,
         # three without) + four epilogue warps x {32 px, 32 channel} boxes
-        # (two output boxes, plus three residual slots) + barriers + slack.
+        # (two output boxes, plus four residual slots) + barriers + slack.
         residual = op_type.endswith("AddRelu")
-        return (2 if residual else 3) * 65536 + 4 * (5 if residual else 2) * 4096 + 256 + 1024
+        return (2 if residual else 3) * 65536 + 4 * (6 if residual else 2) * 4096 + 256 + 1024
 
     return [KernelSpec(kernel_id=kernel_id, op_type=op_type, version=1, source="conv1x1_mn.cu", symbol=symbol,
                        arguments=arguments, grid=grid, layout="NCHW", constraints=constraints,

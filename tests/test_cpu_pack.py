@@ -209,19 +209,19 @@ def test_launch_shapes_match_the_kernels():
 def test_conv1x1_mn_shared_memory_matches_the_kernel():
     """The output-channels-on-M 1x1 kernel: 10 warps, and shared memory for
     its stages (three without a residual, two with one; 64 KB each) and the
-    epilogue boxes (two output boxes per warp, plus three residual slots)."""
+    epilogue boxes (two output boxes per warp, plus four residual slots)."""
     from cutriton_b200 import kernel_specs
 
     source = (Path(kernel_specs.__file__).resolve().parent / "csrc" / "kernels" / "conv1x1_mn.cu").read_text()
     assert "kStages = kResidual ? 2 : 3" in source
-    assert _kernel_constant(source, "kMaxResSlots") == 3 and _kernel_constant(source, "kOutSlots") == 2
+    assert _kernel_constant(source, "kMaxResSlots") == 4 and _kernel_constant(source, "kOutSlots") == 2
     assert _kernel_constant(source, "kEpiWarps") == 4
     specs = [s for s in kernel_specs.all_specs() if s.source == "conv1x1_mn.cu"]
     assert len(specs) == 4
     for spec in specs:
         residual = spec.op_type.endswith("AddRelu")
         stage = 2 * (128 * 32 * 4) + 2 * (4 * 32 * 32 * 4)  # W_hi, W_lo, X_hi, X_lo
-        epilogue = 4 * ((3 if residual else 0) + 2) * 32 * 32 * 4
+        epilogue = 4 * ((4 if residual else 0) + 2) * 32 * 32 * 4
         need = (2 if residual else 3) * stage + epilogue + 1024
         (variant,) = spec.variants
         assert variant.num_warps == 10
