@@ -42,7 +42,7 @@ PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 RN_BATCH_PER_GPU = 256
 UNFUSED = "unfused:"  # candidate-id prefix of the unfused decompositions
-CONV_DRAM_BYTES_PER_STEP_BS256 = 25.685e9  # ncu, the 53 conv kernels of one tuned bs256 step (see roofline.traffic)
+CONV_DRAM_BYTES_PER_STEP_BS256 = 25.669e9  # ncu, the 53 conv kernels of one tuned bs256 step (see roofline.traffic)
 FFN = dict(tokens=4096, hidden=768, inner=3072)
 
 
