@@ -8,10 +8,9 @@
 // the NCHW 1x1 layers. In NCHW the activation plane of one input channel is
 // contiguous along px, so X is an MN-major B operand that TMA copies straight
 // from global memory ({32 px, 32 ci} boxes, 128-byte swizzle with 32-byte
-// atoms) — no gather —
-// and the output of one channel is contiguous along px too: the epilogue
-// thread of TMEM lane co holds 32 consecutive pixels of its channel and
-// leaves them through a {32 px, 32 co} tensor store.
+// atoms) — no gather — and the output of one channel is contiguous along px
+// too: the epilogue thread of TMEM lane co holds 32 consecutive pixels of
+// its channel and leaves them through a {32 px, 32 co} tensor store.
 //
 // 3xTF32: W arrives prepacked as exact TF32 hi / lo planes
 // (conv_w_tf32x2_cb); four split warps turn each landed X block into
@@ -47,7 +46,7 @@ constexpr int kEpiWarp0 = 6;
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr uint32_t kWPlane = kBM * kBK * 4;  // 16 KB: W_hi or W_lo, K-major rows of 128 B
-constexpr uint32_t kBox = 32 * 32 * 4;        // 4 KB: {32 px, 32 channels}, 128-byte swizzle
+constexpr uint32_t kBox = 32 * 32 * 4;        // 4 KB: {32 px, 32 channels}, rows of 128 B
 constexpr uint32_t kXBytes = (kBN / 32) * kBox;  // 16 KB: four pixel boxes of one k block
 constexpr uint32_t kStageBytes = 2 * kWPlane + 2 * kXBytes;
 constexpr int kMaxResSlots = 4;
