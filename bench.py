@@ -70,8 +70,9 @@ def parse_args() -> argparse.Namespace:
     return p.parse_args()
 
 
-def _conv_case(n, c, h, k, r, stride, pad, op="FusedConvBatchNormRelu", residual=False):
-    """One convolution node through the engine; returns (engine, ctx, tensors)."""
+def _conv_case(n, c, h, k, r, stride, pad, op="FusedConvBatchNormRelu", residual=False, **engine_options):
+    """One convolution node through the engine; returns (engine, ctx, tensors).
+    Default: no CUDA graph, no tuning (the default candidate)."""
     import torch
     import cutriton_b200 as ct
 
@@ -90,7 +91,7 @@ def _conv_case(n, c, h, k, r, stride, pad, op="FusedConvBatchNormRelu", residual
     m.add_node("conv", op, names, ["y"], strides=[stride, stride],
                pads=[pad] * 4, dilations=[1, 1], batchnorm_epsilon=1e-5)
     m.add_output("y")
-    e = ct.build_engine(m, enable_cuda_graph=False, tuning_mode=ct.TUNING_DISABLED)
+    e = ct.build_engine(m, **{"enable_cuda_graph": False, "tuning_mode": ct.TUNING_DISABLED, **engine_options})
     ctx = e.create_context()
     x = torch.randn(n, c, h, h, device="cuda")
     y = torch.empty(n, k, ho, ho, device="cuda")
@@ -364,14 +365,27 @@ def run_config2(args, tuning: str = "TuneOnMiss") -> dict:
 
 
 def run_config3(args, peaks) -> dict:
-    """Config 3: one FusedConvBatchNormRelu graph per distinct ResNet-50 conv shape at N=256."""
+    """Config 3: one FusedConvBatchNormRelu graph per distinct ResNet-50 conv
+    shape at N=256, on the candidate the tuner picks (--tuning TuneOnMiss, the
+    default; the warm-up runs tune) or the default one (--tuning Disabled).
+    Device time of the op: the engine's per-op events inside the captured
+    graph, median over the timed runs."""
     import torch
 
     peak_tf = peaks["bf16_tflops"] / 6.0  # burst: each layer runs for well under a millisecond
     rows = []
+    tuning = bench_tuning(args, 0)
+    stream = torch.cuda.Stream()
     for cin, cout, kernel, stride, pad, h in conv_shapes():
-        e, ctx, keep = _conv_case(256, cin, h, cout, kernel, stride, pad)
-        ms = time_context(ctx, torch.cuda.Stream(), args.steps, args.warmup)
+        e, ctx, keep = _conv_case(256, cin, h, cout, kernel, stride, pad, enable_cuda_graph=True,
+                                  enable_profiling=True, **tuning)
+        samples = []
+        for step in range(max(3, args.warmup) + args.steps):
+            ctx.run_async(stream.cuda_stream)
+            ctx.synchronize()
+            if step >= max(3, args.warmup):
+                samples.append(ctx.profile_events()[0][1])
+        ms = float(np.median(samples))
         ho = (h + 2 * pad - kernel) // stride + 1
         flops = 2.0 * 256 * ho * ho * cout * cin * kernel * kernel
         nbytes = 4.0 * 256 * (cin * h * h + cout * ho * ho)
@@ -382,6 +396,7 @@ def run_config3(args, peaks) -> dict:
         del ctx, e, keep
     return {"metric": "per-layer FusedConvBatchNormRelu sweep, N=256 (config 3)", "unit": "TFLOP/s",
             "peak_basis": f"3xTF32 = bf16_tflops (burst) / 6 = {peak_tf:.1f} TFLOP/s; HBM {peaks['hbm_gbs']} GB/s",
+            "tuning": args.tuning, "timing": "per-op CUDA events inside the captured graph, median",
             "layers": rows}
 
 
