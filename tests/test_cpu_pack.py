@@ -98,6 +98,22 @@ def test_unsafe_manifest_entries_are_rejected(relu_model, assume_sm100, tmp_path
     assert err.value.code == ct.INVALID_ARGUMENT
 
 
+@pytest.mark.parametrize("swizzle,atom", [(128, 64), (64, 32)])
+def test_tensor_map_swizzle_atom_is_validated(relu_model, assume_sm100, tmp_path, swizzle, atom):
+    """swizzle_atom (32-byte atoms of the 128-byte swizzle) is accepted only
+    as 32 with a 128-byte swizzle; anything else fails the pack load."""
+    pack = copy_pack(tmp_path)
+    doc = json.loads((pack / "pack.json").read_text())
+    maps = [a["source"] for k in doc["kernels"] for a in k["arguments"] if a["source"]["kind"] == "tensor_map"]
+    assert any(m.get("swizzle_atom") == 32 and m.get("swizzle") == 128 for m in maps)
+    maps[0]["swizzle"] = swizzle
+    maps[0]["swizzle_atom"] = atom
+    (pack / "pack.json").write_text(json.dumps(doc))
+    with pytest.raises(ct.CutritonError) as err:
+        ct.build_engine(relu_model, kernel_artifact_dir=str(pack))
+    assert err.value.code == ct.INVALID_ARGUMENT
+
+
 def test_abi_v1_grid_is_accepted(relu_model, assume_sm100, tmp_path):
     pack = copy_pack(tmp_path)
     doc = json.loads((pack / "pack.json").read_text())
@@ -131,6 +147,10 @@ def test_sdk_validates_specs():
         kernel_sdk.KernelSpec(**{**base.__dict__, "constraints": ({"kind": "lambda"},)}),
         kernel_sdk.KernelSpec(**{**base.__dict__, "arguments": (kernel_sdk.Arg(
             "x", "*fp32", {"kind": "input", "index": 0, "prepack": "unknown"}),) + base.arguments[1:]}),
+        # 32-byte swizzle atoms exist only for the 128-byte swizzle.
+        kernel_sdk.KernelSpec(**{**base.__dict__, "arguments": (kernel_sdk.Arg(
+            "m", "tensormap", {"kind": "tensor_map", "tensor": "input", "index": 0, "box": [32, 32],
+                               "swizzle": 64, "swizzle_atom": 32}),) + base.arguments[1:]}),
     ]
     for spec in bad:
         with pytest.raises(ValueError):
