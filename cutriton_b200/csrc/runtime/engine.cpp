@@ -491,6 +491,7 @@ Status ExecutionContext::PrepareTuning() {
       target.device_id = device_id;
       target.tensors = &s.tensors;
       target.error_word = s.device == nullptr ? nullptr : s.device->error_word_device();
+      if (s.device != nullptr) target.take_device_error = [&s] { return s.device->TakeDeviceError(); };
       target.modules = modules;
       std::vector<double> medians;
       CUTRITON_RETURN_IF_ERROR(runtime::TuneCandidates(target, config, &chosen[i], &medians));

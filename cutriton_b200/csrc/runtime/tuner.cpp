@@ -253,6 +253,16 @@ Status TuneCandidates(const TuningTarget& target, const TuningConfig& config, st
     if (kernels[c].empty()) continue;
     for (int w = 0; w < std::max(1, config.warmup_iterations); ++w) CUTRITON_RETURN_IF_ERROR(launch(c));
     CUTRITON_RETURN_IF_ERROR(drv::Check(api.cuStreamSynchronize(timer.stream), "cuStreamSynchronize"));
+    // A candidate whose kernel reported an error (a shape or alignment
+    // outside its contract, an abandoned wait) is not eligible; the default
+    // candidate's error is the op's error.
+    if (target.take_device_error) {
+      const Status device = target.take_device_error();
+      if (!device.ok()) {
+        if (c == fallback) return device;
+        continue;
+      }
+    }
     std::vector<double> produced;
     CUTRITON_RETURN_IF_ERROR(ReadBack(output, &produced));
     if (c == fallback) {
@@ -282,6 +292,7 @@ Status TuneCandidates(const TuningTarget& target, const TuningConfig& config, st
       samples[c].push_back(ms);
     }
   }
+  if (target.take_device_error) CUTRITON_RETURN_IF_ERROR(target.take_device_error());
   median_ms->assign(op.candidates.size(), std::numeric_limits<double>::infinity());
   for (std::size_t c : eligible) {
     auto& s = samples[c];

@@ -17,6 +17,8 @@
 // thermal drift hit them alike; the median decides. Another candidate
 // replaces the default only when it is faster by more than the noise margin.
 
+#include <functional>
+#include <memory>
 #include <optional>
 #include <string>
 #include <unordered_map>
@@ -43,6 +45,9 @@ struct TuningTarget {
   int device_id{0};
   std::unordered_map<std::string, Tensor>* tensors{nullptr};
   void* error_word{nullptr};
+  // Reads and clears the device error word (after a synchronize); a non-OK
+  // status means a kernel of the candidate just run reported an error.
+  std::function<Status()> take_device_error;
   std::shared_ptr<CudaModuleCache> modules;
 };
 

@@ -156,6 +156,47 @@ def test_tuning_cache_written_once(cuda, tmp_path):
     assert {f.name: f.stat().st_mtime_ns for f in tmp_path.glob("*.json")} == stamps
 
 
+def test_tuner_skips_a_candidate_that_reports_an_error(cuda, tmp_path):
+    """A 1x1 conv whose input is bound 4 bytes past a 16-byte boundary: the
+    output-channels-on-M candidate rejects the binding (it reports a shape
+    error instead of computing), so TuneOnMiss must leave it out, clear the
+    error and run the op on a candidate that handles the binding."""
+    import torch
+
+    rng = np.random.default_rng(5)
+    n, c, h, k = 2, 64, 8, 128
+    x = rng.standard_normal((n, c, h, h)).astype(np.float32)
+    w = (rng.standard_normal((k, c, 1, 1)) * 0.1).astype(np.float32)
+    bn = [rng.uniform(0.5, 1.5, k).astype(np.float32), (rng.standard_normal(k) * 0.1).astype(np.float32),
+          (rng.standard_normal(k) * 0.1).astype(np.float32), rng.uniform(0.5, 1.5, k).astype(np.float32)]
+    model = ct.Model()
+    model.add_input("x", [n, c, h, h])
+    model.add_constant("w", w, layout="OIHW")
+    for name, value in zip(("s", "b", "m", "v"), bn):
+        model.add_constant(name, value, layout="")
+    model.add_node("conv", "FusedConvBatchNormRelu", ["x", "w", "s", "b", "m", "v"], ["y"], strides=[1, 1],
+                   pads=[0, 0, 0, 0], dilations=[1, 1], batchnorm_epsilon=1e-5)
+    model.add_output("y")
+    engine = ct.build_engine(model, enable_cuda_graph=False, tuning_mode=ct.TUNING_TUNE_ON_MISS,
+                             tuning_cache_dir=str(tmp_path), tuning_warmup_iterations=1,
+                             tuning_measurement_iterations=3)
+    assert any("tcgen05_mn" in cand for cand in engine.ops()[0]["candidates"])
+    flat = torch.empty(x.size + 1, device=cuda)
+    xd = flat[1:].view(n, c, h, h)  # 4 bytes past the allocation's alignment
+    xd.copy_(torch.from_numpy(x))
+    assert xd.data_ptr() % 16 == 4
+    y = torch.empty(n, k, h, h, device=cuda)
+    ctx = engine.create_context()
+    ctx.bind_tensor("x", xd)
+    ctx.bind_tensor("y", y, output=True)
+    ctx.run()
+    chosen = engine.ops()[0]["candidates"][ctx.selected_candidate(0)]
+    assert "tcgen05_mn" not in chosen, chosen
+    expected = oracle.conv2d(x, w, bn=bn, relu=True)
+    assert_close(y.cpu().numpy(), expected, atol=1e-4, rtol=1e-4, what=f"tuned around the misaligned input ({chosen})")
+    ctx.run()  # the error word was cleared: a second run is clean too
+
+
 def ffn17_model(golden):
     model = ct.Model()
     model.add_input("x", [17, 128], dtype=np.float16, layout="")
